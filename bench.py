@@ -1,0 +1,367 @@
+"""Benchmark of the SOL routed-attention hot path (pool -> threshold -> fused attention).
+
+Workload (BASELINE metric): video-DiT self-attention B=1, T=32768, H=24, D=128 BF16,
+block-smooth with drift (sigma=0.3), beta=1.0, kv/query sinks 128/128, local_blocks=1,
+seeded synthetic inputs (no captured activations exist here).  Heads are sharded across the
+N ranks (one process per GPU, torchrun); there is no collective on the hot path: NCCL only
+reduces the per-rank timings and gathers exact-block counts after the timed region.
+
+One JSON line on rank 0:
+  value        dense-equivalent TFLOPS of the whole job (4*B*H*Tq*Tk*D / max-over-ranks ms)
+  ms_per_step  max over ranks of the mean device time of one call (inputs resident in HBM)
+  e2e          the same metric through the public API from pinned host buffers, with the
+               host->device copies of Q/K/V and the device->host copy of the output timed
+  roofline     the fused attention kernel against the measured BF16 tensor peak
+  cpu_baseline the CPU oracle port timed on a bounded sample (rank 0, N=1)
+
+``--impl reference`` times the CPU oracle port (the reference's FP32 Torch oracle
+restated in oracle/sol_oracle.py) on the host cores instead; only rank 0 works.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "solattn-amd_b200"))
+
+import torch  # noqa: E402
+
+B, T, H, D = 1, 32768, 24, 128
+BETA, SINK, LOCAL = 1.0, 128, 1
+DENSE_FLOPS = 4.0 * B * H * T * T * D  # dense-equivalent FLOPs of one full call
+METRIC = "ms/call & dense-equiv TFLOPS, T=32k H=24 D=128 bf16, 1/2/4/8 B200; density; err"
+UNIT = "TFLOPS (dense-equivalent)"
+WORKLOAD = ("video_dit self-attention B=1 T=32768 H=24 D=128 bf16, block-smooth drift sigma=0.3, "
+            "beta=1.0, sinks 128/128, local_blocks=1, seed 0")
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / "ncu_traffic.txt"
+    try:
+        for line in f.read_text().splitlines():
+            if line.startswith("attention_bytes_per_launch="):
+                return float(line.split("=", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, indices):
+        self.indices = set(indices)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.rows = []
+        if self.proc is None:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 9 and parts[0].isdigit() and int(parts[0]) in self.indices:
+                self.rows.append(parts)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, val in zip(names, r[5:9]) if val == "Active"})
+        loaded = sorted(sm)[len(sm) // 4:] or sm  # drop idle samples at the edges
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def make_inputs():
+    from sol_attn_b200 import workloads
+    return workloads.video_dit(b=B, t=T, h=H, d=D, sigma=0.3, seed=0)
+
+
+def shard(rank, world):
+    per = H // world
+    return rank * per, (rank + 1) * per
+
+
+def time_cpu_oracle(qh, kh, vh, n_qblocks, threads, heads=(0,)):
+    """Oracle port on ``heads`` and ``n_qblocks`` evenly spaced q-blocks of each; the time is
+    extrapolated linearly to the whole call (all heads, all q-blocks).
+
+    Returns (seconds per full call, sample description, (blocks, output, counts) of head 0)."""
+    from oracle.sol_oracle import sol_oracle
+    torch.set_num_threads(threads)
+    nqb = (T + 63) // 64
+    blocks = sorted(set(int(i * nqb / n_qblocks) for i in range(n_qblocks)))
+    kw = dict(beta=BETA, local_blocks=LOCAL, kv_sink_tokens=SINK, query_sink_tokens=SINK)
+    t_head = t_blocks = 0.0
+    first = None
+    for h in heads:
+        q1, k1, v1 = (x[:, :, h:h + 1].contiguous() for x in (qh, kh, vh))
+        t0 = time.perf_counter()
+        sol_oracle(q1, k1, v1, query_blocks=[], **kw)  # pooling + moments + cutoffs of one head
+        t1 = time.perf_counter()
+        out, counts = sol_oracle(q1, k1, v1, query_blocks=blocks, **kw)
+        t2 = time.perf_counter()
+        t_head += t1 - t0
+        t_blocks += (t2 - t1) - (t1 - t0)
+        if first is None:
+            first = (blocks, out, counts)
+    per_head = t_head / len(heads)
+    per_block = max(t_blocks, 0.0) / (len(heads) * len(blocks))
+    per_call = H * per_head + H * nqb * per_block
+    sample = (f"heads {list(heads)}, {len(blocks)} of {nqb} q-blocks each (+ pooling of those "
+              f"heads), extrapolated linearly to {H} heads x {nqb} q-blocks")
+    return per_call, sample, first
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    qh, kh, vh = make_inputs()
+    n_qb = 128
+    for _ in range(args.warmup):
+        time_cpu_oracle(qh, kh, vh, 8, threads)
+    calls = []
+    sample = ""
+    for _ in range(args.steps):
+        per_call, sample, _ = time_cpu_oracle(qh, kh, vh, n_qb, threads)
+        calls.append(per_call)
+    ms = statistics.mean(calls) * 1e3
+    value = DENSE_FLOPS / (ms * 1e-3) / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded block-smooth drift inputs)",
+            "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "heads": H,
+                       "head_dim": D, "parallelism": "host CPU, oracle port"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if H % world:
+        raise SystemExit(f"{H} heads do not shard over {world} ranks")
+
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from sol_attn_b200 import sol_attention
+    from sol_attn_b200.stages import Stages
+
+    qh, kh, vh = make_inputs()
+    h0, h1 = shard(rank, world)
+    qd, kd, vd = (x.to(dev) for x in (qh, kh, vh))
+    q, k, v = (x[:, :, h0:h1] for x in (qd, kd, vd))  # strided head shard, no copy
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    kw = dict(beta=BETA, local_blocks=LOCAL, kv_sink_tokens=SINK, query_sink_tokens=SINK)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    # ---------------- device-resident timing through the public API ----------------
+    for _ in range(args.warmup):
+        sol_attention(q, k, v, **kw)
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    gpu_ids = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
+    phys = gpu_ids[local_rank] if gpu_ids else local_rank
+    with Clocks([phys] if world == 1 else (gpu_ids[:world] if gpu_ids else range(world))) as clk:
+        barrier()
+        for s, e in ev:
+            flush.zero_()  # inputs per rank can fit in L2 at N=8: flush between steps
+            s.record()
+            sol_attention(q, k, v, **kw)
+            e.record()
+        barrier()
+    step_ms = [s.elapsed_time(e) for s, e in ev]
+    ms = statistics.mean(step_ms)
+
+    # ---------------- per-kernel timing (same kernels, stage by stage) ----------------
+    st = Stages(q, k, v, beta=BETA, local=LOCAL, kv_sink_blocks=SINK // 64, q_sink_blocks=SINK // 64)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        st.run(stream.cuda_stream)
+    n_rep = max(3, args.steps // 2)
+    kt = {"pool": [], "threshold": [], "attention": []}
+    for _ in range(n_rep):
+        flush.zero_()
+        e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+        e0.record(stream)
+        st.pool(stream.cuda_stream)
+        e1.record(stream)
+        st.threshold(stream.cuda_stream)
+        e2.record(stream)
+        st.attention(stream.cuda_stream)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        kt["pool"].append(e0.elapsed_time(e1))
+        kt["threshold"].append(e1.elapsed_time(e2))
+        kt["attention"].append(e2.elapsed_time(e3))
+    k_ms = {n: statistics.mean(v_) for n, v_ in kt.items()}
+    counts = st.counts.clone()
+
+    # ---------------- end-to-end from pinned host buffers ----------------
+    hq, hk, hv = (x[:, :, h0:h1].contiguous().pin_memory() for x in (qh, kh, vh))
+    hout = torch.empty((B, T, h1 - h0, D), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = (torch.empty_like(x, device=dev) for x in (hq, hk, hv))
+    e2e_steps = max(3, args.steps // 2)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        out = sol_attention(dq, dk, dv, **kw)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(e2e_steps)]
+    for s, e in e2e_ev:
+        flush.zero_()
+        s.record()
+        e2e_step()
+        e.record()
+    barrier()
+    e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in e2e_ev)
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+    d2h = hout.numel() * hout.element_size()
+
+    # ---------------- reduce over ranks (after timing) ----------------
+    vals = torch.tensor([ms, e2e_ms, k_ms["pool"], k_ms["threshold"], k_ms["attention"]],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        gathered = [torch.empty_like(counts) for _ in range(world)]
+        dist.all_gather(gathered, counts)
+        counts_all = torch.cat(gathered, dim=2)
+    else:
+        counts_all = counts
+    ms, e2e_ms, pool_ms, thr_ms, attn_ms = vals.tolist()
+
+    nkb = nqb = T // 64
+    total_exact = int(counts_all.sum())
+    density = total_exact / (B * H * nqb * nkb)
+    # Algorithmic FLOPs of the fused kernel on this rank's shard: every selected block is a
+    # 64x64 exact tile (T is a multiple of 64), every unselected block one centroid column.
+    my_exact = int(counts.sum())
+    my_units = B * (h1 - h0) * nqb
+    attn_flops = 4.0 * D * 64 * (64 * my_exact + (my_units * nkb - my_exact))
+    pk, pk_kind = peaks()
+    attn_tflops = attn_flops / (k_ms["attention"] * 1e-3) / 1e12
+    pool_bytes = 3 * B * T * (h1 - h0) * D * 2 + B * (h1 - h0) * (2 * nkb * D * 2 + nqb * D * 4)
+    pool_gbs = pool_bytes / (k_ms["pool"] * 1e-3) / 1e9
+
+    result = None
+    if rank == 0:
+        err = None
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            per_call, sample, (blocks, ref, _) = time_cpu_oracle(qh, kh, vh, 512, threads,
+                                                                 heads=(0, 8, 16))
+            cpu = {"value": DENSE_FLOPS / per_call / 1e12, "unit": UNIT, "cores": threads,
+                   "kind": "port", "sample": sample, "seconds_per_call": per_call}
+        else:
+            _, _, (blocks, ref, _) = time_cpu_oracle(qh, kh, vh, 4, os.cpu_count() or 1)
+        got = st.out[:, :, 0:1].float().cpu()
+        rows = torch.cat([torch.arange(b * 64, b * 64 + 64) for b in blocks])
+        delta = (got[:, rows] - ref[:, rows]).abs()
+        err = {"max_abs": float(delta.max()),
+               "mean_rel": float(delta.sum() / ref[:, rows].abs().sum()),
+               "rel_l2": float((got[:, rows] - ref[:, rows]).norm() / ref[:, rows].norm()),
+               "vs": "CPU oracle, head 0, sampled q-blocks", "q_blocks": len(blocks)}
+        result = {
+            "metric": METRIC, "value": DENSE_FLOPS / (ms * 1e-3) / 1e12, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded block-smooth drift inputs, no captured activations)",
+            "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "heads": H,
+                       "head_dim": D, "parallelism": f"head-sharded x{world}",
+                       "l2": "flushed between timed steps (256 MiB write), inputs 604 MB"},
+            "density": density, "err": err,
+            "kernel_ms": {"pool": pool_ms, "threshold": thr_ms, "attention": attn_ms},
+            "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": attn_tflops / pk["bf16_tflops"],
+                         "traffic": ncu_traffic(), "kernel": "attention (fused routed)",
+                         "algorithmic_flops_per_launch": attn_flops, "peak_source": pk_kind},
+            "pool_roofline": {"bound": "hbm", "achieved": pool_gbs, "peak": pk["hbm_gbs"],
+                              "unit": "GB/s", "frac": pool_gbs / pk["hbm_gbs"],
+                              "bytes_per_launch": pool_bytes, "peak_source": pk_kind},
+            "cpu_baseline": cpu,
+            "e2e": {"value": DENSE_FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+                    "ms_per_call": e2e_ms, "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": st.launches() * args.steps * world,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,165 @@
+/*
+ * solattn.h - C ABI of the B200 (sm_100a) SOL routed block-sparse attention library
+ * (libsolattn.so).
+ *
+ * Every entry point takes raw device pointers, sizes, element strides, scalars and a
+ * CUDA stream passed as `void*` (a cudaStream_t; NULL is the legacy default stream). No
+ * entry point allocates, synchronises or keeps state between calls: buffers are owned by
+ * the caller (in the Python layer, torch). Work is enqueued on `stream` asynchronously.
+ * Return value: SOLATTN_OK (0) or a negative SOLATTN_ERR_* code; solattn_strerror() gives
+ * the message. Errors that a kernel detects on the device (a bounded wait that ran out, an
+ * index outside its tensor) are written to the caller's status word (see
+ * solattn_workspace_layout) and read with solattn_read_status().
+ *
+ * Tensor conventions (mirroring zihaomu/SolAttn-AMD):
+ *   - BTHD activations q [B, Tq, H, D], k and v [B, Tk, H, D], BF16, any positive element
+ *     strides (sB, sT, sH) with a contiguous head dimension (attention.py:37-38).
+ *   - Indexed (NHD) activations [N, H, D] are passed with B = windows, sB = 0 and a gather
+ *     index per tensor: token t of window w is row q_idx[w*Tq + t] (resp. kv_idx[w*Tk + t])
+ *     of the NHD tensor (indexed.py:99); idx_rows = N.  An index outside [0, N) is reported
+ *     in the status word (kernels read row 0 instead).
+ *   - Blocks are 64 tokens; nqb = ceil(Tq/64), nkb = ceil(Tk/64).
+ *   - Output is a fresh contiguous [B, Tq, H, D] BF16 tensor (kernels.py:179-180);
+ *     counts is int32 [B, nqb, H] (kernels.py:181-182, attention.py:10-16).
+ */
+#ifndef SOLATTN_H_
+#define SOLATTN_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SOLATTN_API __attribute__((visibility("default")))
+#else
+#define SOLATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SOLATTN_OK 0
+#define SOLATTN_ERR_ARG (-1)         /* invalid argument (shape, stride, alignment, pointer) */
+#define SOLATTN_ERR_UNSUPPORTED (-2) /* valid but not implemented here (e.g. D not 64/128) */
+#define SOLATTN_ERR_LAUNCH (-3)      /* CUDA reported an error at launch */
+#define SOLATTN_ERR_DEVICE (-4)      /* a kernel reported a device-side error in the status word */
+#define SOLATTN_ERR_CUDA (-5)        /* a CUDA runtime call failed */
+
+/* Routing force modes (kernels.py:208): 0 threshold, 1 all blocks exact (beta=-inf),
+ * 2 only protected blocks exact (beta=+inf). */
+#define SOLATTN_FORCE_THRESHOLD 0
+#define SOLATTN_FORCE_ALL 1
+#define SOLATTN_FORCE_NONE 2
+
+/* Library version string, e.g. "sol-attn-b200 0.1.0 sm_100a". */
+SOLATTN_API const char* solattn_version(void);
+
+/* Message for a SOLATTN_* code. */
+SOLATTN_API const char* solattn_strerror(int code);
+
+/*
+ * Scratch layout of one forward call.  Replaces the torch.empty allocations of the
+ * reference launcher (kernels.py:185-190, 203-217): kc/vc (BF16 K/V block means), qc (FP32
+ * Q block means), mean/var (FP32 key moments), cutoff (FP32 Eq. 15 thresholds) and one
+ * device status word.  Offsets are in bytes from the workspace base, each 256-byte aligned.
+ * The pooled tensors use the layout [B, H, blocks, D]; cutoff is [B, H, nqb].
+ * Returns the total size in bytes, or 0 on an invalid shape.
+ */
+SOLATTN_API int64_t solattn_workspace_layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                                 int64_t* off_kc, int64_t* off_vc, int64_t* off_qc,
+                                 int64_t* off_mean, int64_t* off_var, int64_t* off_cutoff,
+                                 int64_t* off_status);
+
+/*
+ * Block pooling of Q, K and V in one launch.  Replaces `_pooled`/`_pool`
+ * (kernels.py:16-27, 185-190): per 64-token block and head, the FP32 mean over the valid
+ * rows min(64, T - 64*blk) (the ragged tail uses its own count).  K and V means are stored
+ * as BF16 (round to nearest even), Q means as FP32.  With pool_q = 0 the Q pass is skipped
+ * (beta = +-inf, kernels.py:209).  q_idx / kv_idx are NULL for BTHD or the indexed gather
+ * indices described above.
+ * Summation order (fixed, deterministic): 8 row groups; group g sums rows g, g+8, ..., g+56
+ * in order; the 8 group sums are then added in order g = 0..7; mean = sum / count (IEEE).
+ */
+SOLATTN_API int solattn_pool_qkv(const void* q, const void* k, const void* v,
+                     int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                     int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                     int64_t k_sB, int64_t k_sT, int64_t k_sH,
+                     int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                     const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows, int pool_q,
+                     float* qc, void* kc, void* vc, int32_t* status, void* stream);
+
+/*
+ * Key moments and Eq. 15 thresholds.  Replaces `_moments` + `_threshold`
+ * (kernels.py:30-64, launches 211-215): per (b, h, d) mean = sum(kc)/nkb and
+ * var = max(sum(kc^2)/nkb - mean^2, 0) over all key blocks, unweighted (sequential FP32
+ * sums over blocks); per (b, h, q-block)
+ * cutoff = (sum_d qc*mean + beta * sqrt(sum_d (qc*qc)*var)) * scale with sequential FP32
+ * sums over d.  The cutoff is in natural-log units: the attention kernel selects key block j
+ * iff (sum_d qc[d]*kc_j[d]) * scale > cutoff, every operation rounded to nearest FP32, no
+ * fused multiply-add.  beta must be finite.
+ */
+SOLATTN_API int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int64_t nqb,
+                      int64_t nkb, int64_t D, float scale, float beta, float* mean, float* var,
+                      float* cutoff, void* stream);
+
+/*
+ * Fused routed attention.  Replaces `_sol` (kernels.py:101-182, launch 216-224): per
+ * (b, h, 64-row q-block) it routes every key block (threshold / force mode, OR the local
+ * rule |kb-qb| <= local (local < 0 disables it), kb < kv_sink_blocks, qb < q_sink_blocks
+ * and protected[b, qb, kb] when `protect` is not NULL), computes the selected blocks exactly
+ * (BF16 QK and PV, FP32 online softmax) and folds every unselected block in through its
+ * centroid (logit q.kc*scale + log(len), value vc).  cutoff and qc may be NULL when
+ * force != 0.  counts may be NULL.  status may be NULL.
+ * debug_mask (NULL in normal use) receives the kernel's own routing decisions as a bitmask
+ * [B, H, nqb, ceil(nkb/32)] of uint32 words (bit kb%32 of word kb/32 set = block kb exact);
+ * it exists only so tests can compare routing bit for bit and is never written otherwise.
+ */
+SOLATTN_API int solattn_attention(const void* q, const void* k, const void* v,
+                      int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                      int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                      int64_t k_sB, int64_t k_sT, int64_t k_sH,
+                      int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                      const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                      const void* kc, const void* vc, const float* qc, const float* cutoff,
+                      const uint8_t* protect, float scale, int force, int local,
+                      int kv_sink_blocks, int q_sink_blocks, void* out, int32_t* counts,
+                      int32_t* status, uint32_t* debug_mask, void* stream);
+
+/*
+ * All-in SOL forward: pool -> threshold (force == 0 only) -> fused attention, the whole of
+ * `launch_sol` (kernels.py:203-225), using the caller's workspace of
+ * solattn_workspace_layout() bytes.  beta may be +-inf (selects the force mode) but not NaN.
+ */
+SOLATTN_API int solattn_sol_forward(const void* q, const void* k, const void* v,
+                        int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                        int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                        int64_t k_sB, int64_t k_sT, int64_t k_sH,
+                        int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                        const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                        const uint8_t* protect,
+                        float scale, float beta, int local, int kv_sink_blocks,
+                        int q_sink_blocks, void* workspace, int64_t workspace_bytes,
+                        void* out, int32_t* counts, void* stream);
+
+/*
+ * Dense noncausal attention over all keys (BF16 QK/PV, FP32 softmax).  Replaces
+ * `launch_dense`/`_dense` (kernels.py:67-98, 193-200); implemented as the all-exact route
+ * of the fused kernel, so it needs no workspace.
+ */
+SOLATTN_API int solattn_dense(const void* q, const void* k, const void* v,
+                  int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                  int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                  int64_t k_sB, int64_t k_sT, int64_t k_sH,
+                  int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                  float scale, void* out, void* stream);
+
+/*
+ * Synchronises `stream`, copies the device status word at `status` to the host, clears it
+ * and returns it through *value (0 = no device-side error).  Diagnostic use only: it blocks.
+ */
+SOLATTN_API int solattn_read_status(int32_t* status, int32_t* value, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOLATTN_H_ */

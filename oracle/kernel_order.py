@@ -1,0 +1,115 @@
+"""Bit-exact CPU restatement of the pooled statistics and routing arithmetic of the CUDA
+kernels (TEST INFRASTRUCTURE ONLY; see the header of ``sol_oracle.py`` for who may use it).
+
+The reference (zihaomu/SolAttn-AMD) leaves the FP32 summation order of pooling, moments,
+thresholds and the routing proxy to Triton/BLAS (``kernels.py:16-64, 129-135``;
+``reference.py:13-15, 27-41``), so no implementation reproduces it bit for bit. The CUDA
+kernels of this package fix one order and round every operation to nearest FP32 without
+fused multiply-adds; this module restates that order in numpy float32 so tests can demand
+bit identity:
+
+* pooling (``solattn_pool_qkv``): 8 row groups, group g sums rows g, g+8, ..., g+56 of the
+  block in order (rows past the ragged end skipped), the group sums are added in order
+  g = 0..7, mean = sum / count; K/V means rounded to BF16 (nearest even);
+* moments (``solattn_threshold``): sequential sums over key blocks of x and x*x,
+  mean = s1/n, var = max(s2/n - mean*mean, 0);
+* cutoff: sequential sums over d of qc*mean and (qc*qc)*var,
+  cutoff = (mu + beta*sqrt(sg)) * scale;
+* routing (fused kernel prologue): proxy = (sequential sum over d of qc*kc) * scale,
+  exact iff proxy > cutoff (force modes and the local / sink / protected rules as in
+  ``reference.py:41-51``).
+
+Routing decisions computed here from the GPU's own pooled statistics must equal the GPU's
+bit for bit (the north-star routing criterion).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+BLOCK = 64
+F32 = np.float32
+
+
+def _bf16_round(x: np.ndarray) -> np.ndarray:
+    return torch.from_numpy(np.ascontiguousarray(x)).to(torch.bfloat16).float().numpy()
+
+
+def pool(x: torch.Tensor, out_bf16: bool) -> np.ndarray:
+    """Block means of a BTHD tensor [B, T, H, D] -> [B, H, nb, D] float32 (BF16-rounded if asked)."""
+    B, T, H, D = x.shape
+    nb = (T + BLOCK - 1) // BLOCK
+    pad = nb * BLOCK - T
+    xf = x.float()
+    if pad:
+        xf = torch.cat((xf, torch.zeros((B, pad, H, D))), 1)
+    a = xf.numpy().reshape(B, nb, BLOCK, H, D).transpose(0, 3, 1, 2, 4)  # [B,H,nb,64,D]
+    total = np.zeros((B, H, nb, D), F32)
+    for g in range(8):
+        part = np.zeros((B, H, nb, D), F32)
+        for i in range(8):
+            part = part + a[:, :, :, g + 8 * i]  # zero rows past the end leave sums unchanged
+        total = total + part
+    counts = np.array([min(BLOCK, T - j * BLOCK) for j in range(nb)], F32)
+    mean = total / counts[None, None, :, None]
+    return _bf16_round(mean) if out_bf16 else mean.astype(F32)
+
+
+def moments(kc: np.ndarray):
+    """kc [B, H, nkb, D] (BF16 values as float32) -> mean, var [B, H, D]."""
+    n = F32(kc.shape[2])
+    s1 = np.zeros(kc.shape[:2] + kc.shape[3:], F32)
+    s2 = np.zeros_like(s1)
+    for j in range(kc.shape[2]):
+        x = kc[:, :, j]
+        s1 = s1 + x
+        s2 = s2 + x * x
+    mean = s1 / n
+    var = np.maximum(s2 / n - mean * mean, F32(0))
+    return mean, var
+
+
+def cutoffs(qc: np.ndarray, mean: np.ndarray, var: np.ndarray, beta: float, scale: float):
+    """qc [B, H, nqb, D] -> cutoff [B, H, nqb]."""
+    mu = np.zeros(qc.shape[:3], F32)
+    sg = np.zeros_like(mu)
+    for e in range(qc.shape[3]):
+        qv = qc[..., e]
+        mu = mu + qv * mean[:, :, None, e]
+        sg = sg + (qv * qv) * var[:, :, None, e]
+    return (mu + F32(beta) * np.sqrt(sg)) * F32(scale)
+
+
+def route(qc, kc, cutoff, scale, force, local, kv_sink_blocks, q_sink_blocks, protect=None):
+    """Exact-block selection [B, H, nqb, nkb] (bool) from pooled statistics."""
+    B, H, nqb, D = qc.shape
+    nkb = kc.shape[2]
+    if force == 1:
+        sel = np.ones((B, H, nqb, nkb), bool)
+    elif force == 2:
+        sel = np.zeros((B, H, nqb, nkb), bool)
+    else:
+        dot = np.zeros((B, H, nqb, nkb), F32)
+        for d in range(D):
+            dot = dot + qc[:, :, :, None, d] * kc[:, :, None, :, d]
+        sel = (dot * F32(scale)) > cutoff[..., None]
+    qb = np.arange(nqb)[:, None]
+    kb = np.arange(nkb)[None, :]
+    forced = (kb < kv_sink_blocks) | (qb < q_sink_blocks)
+    if local >= 0:
+        forced = forced | (np.abs(kb - qb) <= local)
+    sel = sel | forced[None, None]
+    if protect is not None:
+        sel = sel | np.asarray(protect, bool)[:, None]
+    return sel
+
+
+def pack_mask(sel: np.ndarray) -> np.ndarray:
+    """bool [..., nkb] -> uint32 words [..., ceil(nkb/32)] (bit kb%32 of word kb//32)."""
+    nkb = sel.shape[-1]
+    nw = (nkb + 31) // 32
+    padded = np.zeros(sel.shape[:-1] + (nw * 32,), bool)
+    padded[..., :nkb] = sel
+    bits = padded.reshape(sel.shape[:-1] + (nw, 32)).astype(np.uint64)
+    return (bits << np.arange(32, dtype=np.uint64)).sum(-1).astype(np.uint32)

@@ -1,0 +1,289 @@
+// extern "C" entry points of libsolattn.so (declared in include/solattn.h).
+// Argument checking here is the C-side contract; the Python layer performs the reference's
+// ValueError validation (attention.py:25-45) before it gets this far.
+#include <math.h>
+#include <stdio.h>
+
+#include "../../include/solattn.h"
+#include "common.cuh"
+
+namespace solattn {
+cudaError_t launch_pool(const PoolParams& p, int D, cudaStream_t stream);
+cudaError_t launch_threshold(const __nv_bfloat16* kc, const float* qc, int BH, int H, int nqb,
+                             int nkb, int D, float scale, float beta, float* mean, float* var,
+                             float* cutoff, cudaStream_t stream);
+cudaError_t launch_attention(const AttnParams& p, int D, cudaStream_t stream);
+}  // namespace solattn
+
+using namespace solattn;
+
+namespace {
+
+constexpr int64_t kMaxTokens = int64_t(1) << 24;  // 16M rows per sequence
+constexpr int64_t kMaxBlocks = 16384;             // key blocks the routing bitmask holds
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Strides are elements; every row start must be 16-byte aligned for the vector loads.
+bool strides_ok(int64_t sB, int64_t sT, int64_t sH) {
+  return sB >= 0 && sT > 0 && sH > 0 && sB % 8 == 0 && sT % 8 == 0 && sH % 8 == 0;
+}
+
+int check_shapes(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
+  if (B <= 0 || Tq <= 0 || Tk <= 0 || H <= 0) return SOLATTN_ERR_ARG;
+  if (D != 64 && D != 128) return SOLATTN_ERR_UNSUPPORTED;
+  if (Tq > kMaxTokens || Tk > kMaxTokens || B * H > (int64_t(1) << 30)) return SOLATTN_ERR_ARG;
+  if (cdiv(Tk, kBlock) > kMaxBlocks) return SOLATTN_ERR_UNSUPPORTED;
+  if (cdiv(Tq, kBlock) > 65535 * 64 || B * H > 65535) return SOLATTN_ERR_UNSUPPORTED;
+  return SOLATTN_OK;
+}
+
+TensorView view(const void* ptr, int64_t sB, int64_t sT, int64_t sH, const int64_t* idx,
+                int64_t rows) {
+  TensorView t;
+  t.ptr = static_cast<const __nv_bfloat16*>(ptr);
+  t.sB = sB;
+  t.sT = sT;
+  t.sH = sH;
+  t.idx = idx;
+  t.rows = rows;
+  return t;
+}
+
+int from_cuda(cudaError_t e) { return e == cudaSuccess ? SOLATTN_OK : SOLATTN_ERR_LAUNCH; }
+
+struct Layout {
+  int64_t kc, vc, qc, mean, var, cutoff, status, total;
+};
+
+Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
+  Layout L;
+  const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
+  int64_t off = 0;
+  L.status = off;
+  off = align256(off + 16);
+  L.kc = off;
+  off = align256(off + B * H * nkb * D * 2);
+  L.vc = off;
+  off = align256(off + B * H * nkb * D * 2);
+  L.qc = off;
+  off = align256(off + B * H * nqb * D * 4);
+  L.mean = off;
+  off = align256(off + B * H * D * 4);
+  L.var = off;
+  off = align256(off + B * H * D * 4);
+  L.cutoff = off;
+  off = align256(off + B * H * nqb * 4);
+  L.total = off;
+  return L;
+}
+
+// Rows of the underlying tensor addressed by a gather index (bounds for the device check).
+int64_t gather_rows(const int64_t* idx, int64_t idx_rows, int64_t T) { return idx ? idx_rows : T; }
+
+}  // namespace
+
+extern "C" {
+
+const char* solattn_version(void) { return "sol-attn-b200 0.1.0 sm_100a"; }
+
+const char* solattn_strerror(int code) {
+  switch (code) {
+    case SOLATTN_OK: return "ok";
+    case SOLATTN_ERR_ARG: return "invalid argument";
+    case SOLATTN_ERR_UNSUPPORTED: return "unsupported configuration";
+    case SOLATTN_ERR_LAUNCH: return "kernel launch failed";
+    case SOLATTN_ERR_DEVICE: return "device-side error reported by a kernel";
+    case SOLATTN_ERR_CUDA: return "CUDA runtime call failed";
+    default: return "unknown error";
+  }
+}
+
+int64_t solattn_workspace_layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                                 int64_t* off_kc, int64_t* off_vc, int64_t* off_qc,
+                                 int64_t* off_mean, int64_t* off_var, int64_t* off_cutoff,
+                                 int64_t* off_status) {
+  if (check_shapes(B, Tq, Tk, H, D) != SOLATTN_OK) return 0;
+  const Layout L = layout(B, Tq, Tk, H, D);
+  if (off_kc) *off_kc = L.kc;
+  if (off_vc) *off_vc = L.vc;
+  if (off_qc) *off_qc = L.qc;
+  if (off_mean) *off_mean = L.mean;
+  if (off_var) *off_var = L.var;
+  if (off_cutoff) *off_cutoff = L.cutoff;
+  if (off_status) *off_status = L.status;
+  return L.total;
+}
+
+int solattn_pool_qkv(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                     int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                     int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT,
+                     int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                     int pool_q, float* qc, void* kc, void* vc, int32_t* status, void* stream) {
+  int rc = check_shapes(B, Tq, Tk, H, D);
+  if (rc) return rc;
+  if (!k || !v || !kc || !vc || (pool_q && (!q || !qc))) return SOLATTN_ERR_ARG;
+  if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
+  if (!aligned16(k) || !aligned16(v) || (pool_q && !aligned16(q))) return SOLATTN_ERR_ARG;
+  if (!strides_ok(k_sB, k_sT, k_sH) || !strides_ok(v_sB, v_sT, v_sH) ||
+      (pool_q && !strides_ok(q_sB, q_sT, q_sH)))
+    return SOLATTN_ERR_ARG;
+  PoolParams p;
+  p.x[0] = view(q, q_sB, q_sT, q_sH, q_idx, gather_rows(q_idx, idx_rows, Tq));
+  p.x[1] = view(k, k_sB, k_sT, k_sH, kv_idx, gather_rows(kv_idx, idx_rows, Tk));
+  p.x[2] = view(v, v_sB, v_sT, v_sH, kv_idx, gather_rows(kv_idx, idx_rows, Tk));
+  p.T[0] = (int)Tq;
+  p.T[1] = p.T[2] = (int)Tk;
+  p.nb[0] = (int)cdiv(Tq, kBlock);
+  p.nb[1] = p.nb[2] = (int)cdiv(Tk, kBlock);
+  p.units[0] = pool_q ? B * p.nb[0] * H : 0;
+  p.units[1] = p.units[2] = B * p.nb[1] * H;
+  p.y[0] = qc;
+  p.y[1] = kc;
+  p.y[2] = vc;
+  p.B = (int)B;
+  p.H = (int)H;
+  p.status = status;
+  return from_cuda(launch_pool(p, (int)D, static_cast<cudaStream_t>(stream)));
+}
+
+int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int64_t nqb,
+                      int64_t nkb, int64_t D, float scale, float beta, float* mean, float* var,
+                      float* cutoff, void* stream) {
+  if (B <= 0 || H <= 0 || nqb <= 0 || nkb <= 0 || nkb > kMaxBlocks) return SOLATTN_ERR_ARG;
+  if (D != 64 && D != 128) return SOLATTN_ERR_UNSUPPORTED;
+  if (!kc || !qc || !mean || !var || !cutoff) return SOLATTN_ERR_ARG;
+  if (!(scale > 0.f) || !isfinite(scale) || !isfinite(beta)) return SOLATTN_ERR_ARG;
+  return from_cuda(launch_threshold(static_cast<const __nv_bfloat16*>(kc), qc, (int)(B * H),
+                                    (int)H, (int)nqb, (int)nkb, (int)D, scale, beta, mean, var,
+                                    cutoff, static_cast<cudaStream_t>(stream)));
+}
+
+int solattn_attention(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                      int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                      int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT,
+                      int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                      const void* kc, const void* vc, const float* qc, const float* cutoff,
+                      const uint8_t* protect, float scale, int force, int local,
+                      int kv_sink_blocks, int q_sink_blocks, void* out, int32_t* counts,
+                      int32_t* status, uint32_t* debug_mask, void* stream) {
+  int rc = check_shapes(B, Tq, Tk, H, D);
+  if (rc) return rc;
+  if (!q || !k || !v || !kc || !vc || !out) return SOLATTN_ERR_ARG;
+  if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
+  if (force < 0 || force > 2 || (force == 0 && (!qc || !cutoff))) return SOLATTN_ERR_ARG;
+  if (!(scale > 0.f) || !isfinite(scale) || kv_sink_blocks < 0 || q_sink_blocks < 0)
+    return SOLATTN_ERR_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(kc) ||
+      !aligned16(vc))
+    return SOLATTN_ERR_ARG;
+  if (!strides_ok(q_sB, q_sT, q_sH) || !strides_ok(k_sB, k_sT, k_sH) ||
+      !strides_ok(v_sB, v_sT, v_sH))
+    return SOLATTN_ERR_ARG;
+  AttnParams p;
+  p.q = view(q, q_sB, q_sT, q_sH, q_idx, gather_rows(q_idx, idx_rows, Tq));
+  p.k = view(k, k_sB, k_sT, k_sH, kv_idx, gather_rows(kv_idx, idx_rows, Tk));
+  p.v = view(v, v_sB, v_sT, v_sH, kv_idx, gather_rows(kv_idx, idx_rows, Tk));
+  p.kc = static_cast<const __nv_bfloat16*>(kc);
+  p.vc = static_cast<const __nv_bfloat16*>(vc);
+  p.qc = qc;
+  p.cutoff = cutoff;
+  p.protect = protect;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.counts = counts;
+  p.status = status;
+  p.debug_mask = debug_mask;
+  p.B = (int)B;
+  p.Tq = (int)Tq;
+  p.Tk = (int)Tk;
+  p.H = (int)H;
+  p.nqb = (int)cdiv(Tq, kBlock);
+  p.nkb = (int)cdiv(Tk, kBlock);
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.force = force;
+  p.local = local;
+  p.kv_sink_blocks = kv_sink_blocks;
+  p.q_sink_blocks = q_sink_blocks;
+  return from_cuda(launch_attention(p, (int)D, static_cast<cudaStream_t>(stream)));
+}
+
+int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                        int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT,
+                        int64_t q_sH, int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB,
+                        int64_t v_sT, int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx,
+                        int64_t idx_rows, const uint8_t* protect, float scale, float beta, int local,
+                        int kv_sink_blocks, int q_sink_blocks, void* workspace,
+                        int64_t workspace_bytes, void* out, int32_t* counts, void* stream) {
+  int rc = check_shapes(B, Tq, Tk, H, D);
+  if (rc) return rc;
+  if (isnan(beta) || !workspace) return SOLATTN_ERR_ARG;
+  // Every argument is checked before the first CUDA call.
+  if (!q || !k || !v || !out || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return SOLATTN_ERR_ARG;
+  if (!strides_ok(q_sB, q_sT, q_sH) || !strides_ok(k_sB, k_sT, k_sH) ||
+      !strides_ok(v_sB, v_sT, v_sH))
+    return SOLATTN_ERR_ARG;
+  if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
+  if (!(scale > 0.f) || !isfinite(scale) || kv_sink_blocks < 0 || q_sink_blocks < 0)
+    return SOLATTN_ERR_ARG;
+  const Layout L = layout(B, Tq, Tk, H, D);
+  if (workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return SOLATTN_ERR_ARG;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int force = isinf(beta) ? (beta < 0 ? SOLATTN_FORCE_ALL : SOLATTN_FORCE_NONE)
+                                : SOLATTN_FORCE_THRESHOLD;
+  const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
+  float* qc = reinterpret_cast<float*>(ws + L.qc);
+  void* kc = ws + L.kc;
+  void* vc = ws + L.vc;
+  float* cutoff = reinterpret_cast<float*>(ws + L.cutoff);
+  int32_t* status = reinterpret_cast<int32_t*>(ws + L.status);
+  if (cudaMemsetAsync(status, 0, sizeof(int32_t), static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return SOLATTN_ERR_CUDA;
+  rc = solattn_pool_qkv(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT,
+                        v_sH, q_idx, kv_idx, idx_rows, force == SOLATTN_FORCE_THRESHOLD, qc, kc, vc,
+                        status, stream);
+  if (rc) return rc;
+  if (force == SOLATTN_FORCE_THRESHOLD) {
+    rc = solattn_threshold(kc, qc, B, H, nqb, nkb, D, scale, beta,
+                           reinterpret_cast<float*>(ws + L.mean),
+                           reinterpret_cast<float*>(ws + L.var), cutoff, stream);
+    if (rc) return rc;
+  }
+  return solattn_attention(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
+                           v_sT, v_sH, q_idx, kv_idx, idx_rows, kc, vc,
+                           force == SOLATTN_FORCE_THRESHOLD ? qc : nullptr,
+                           force == SOLATTN_FORCE_THRESHOLD ? cutoff : nullptr, protect, scale,
+                           force, local, kv_sink_blocks, q_sink_blocks, out, counts, status,
+                           nullptr, stream);
+}
+
+int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,
+                  int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH, int64_t k_sB,
+                  int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                  float scale, void* out, void* stream) {
+  // All-exact route: no pooled statistics are read (kc/vc are only dereferenced for
+  // centroid tiles, and force = 1 produces none), so the K/V pointers stand in for them.
+  return solattn_attention(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
+                           v_sT, v_sH, nullptr, nullptr, 0, k, v, nullptr, nullptr, nullptr, scale,
+                           SOLATTN_FORCE_ALL, -1, 0, 0, out, nullptr, nullptr, nullptr, stream);
+}
+
+int solattn_read_status(int32_t* status, int32_t* value, void* stream) {
+  if (!status || !value) return SOLATTN_ERR_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t host = 0;
+  if (cudaMemcpyAsync(&host, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return SOLATTN_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return SOLATTN_ERR_CUDA;
+  if (cudaMemsetAsync(status, 0, sizeof(int32_t), s) != cudaSuccess) return SOLATTN_ERR_CUDA;
+  *value = host;
+  return host ? SOLATTN_ERR_DEVICE : SOLATTN_OK;
+}
+
+}  // extern "C"

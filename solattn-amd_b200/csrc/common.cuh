@@ -1,0 +1,151 @@
+// Shared device helpers for the SOL attention kernels (sm_100a).
+// Hand-written PTX wrappers: cp.async, ldmatrix, mma.sync (used by the pooling and
+// small-tile paths), ex2, and the launch-parameter structures shared by the host layer.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace solattn {
+
+constexpr int kBlock = 64;  // tokens per routing block (kernels.py:12)
+
+// Device-side error codes written to the caller's status word (first error wins).
+constexpr int kStatusWaitTimeout = 1;  // a bounded mbarrier wait ran out
+constexpr int kStatusBadIndex = 2;     // a gather index outside its tensor
+constexpr int kStatusTmem = 3;         // TMEM allocation returned an unusable address
+
+struct TensorView {
+  const __nv_bfloat16* ptr;
+  int64_t sB, sT, sH;   // element strides; the head dimension is contiguous
+  const int64_t* idx;   // optional gather index [B, T] (indexed NHD inputs), else nullptr
+  int64_t rows;         // number of rows of the underlying tensor (bounds for idx)
+};
+
+struct AttnParams {
+  TensorView q, k, v;
+  const __nv_bfloat16* kc;  // [B, H, nkb, D]
+  const __nv_bfloat16* vc;  // [B, H, nkb, D]
+  const float* qc;          // [B, H, nqb, D]
+  const float* cutoff;      // [B, H, nqb]
+  const uint8_t* protect;   // [B, nqb, nkb] or nullptr
+  __nv_bfloat16* out;       // [B, Tq, H, D]
+  int32_t* counts;          // [B, nqb, H] or nullptr
+  int32_t* status;          // device status word or nullptr
+  uint32_t* debug_mask;     // [B, H, nqb, ceil(nkb/32)] routing bitmask (tests only) or nullptr
+  int B, Tq, Tk, H, nqb, nkb;
+  float scale;       // softmax scale (natural-log units), used by routing
+  float scale_log2;  // scale * log2(e), used by the softmax
+  int force, local, kv_sink_blocks, q_sink_blocks;
+};
+
+struct PoolParams {
+  TensorView x[3];   // q, k, v
+  int T[3];          // Tq, Tk, Tk
+  int nb[3];         // blocks per tensor
+  int64_t units[3];  // units per tensor (B*nb*H); 0 skips the tensor
+  void* y[3];        // qc (float), kc (bf16), vc (bf16)
+  int B, H;
+  int32_t* status;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void report(int32_t* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// Address of token row t of (b, h) in a BTHD view, or of the gathered NHD row.
+__device__ __forceinline__ const __nv_bfloat16* row_ptr(const TensorView& x, int T, int b, int h,
+                                                        int t, int32_t* status) {
+  int64_t tok = t;
+  if (x.idx) {
+    tok = __ldg(x.idx + (int64_t)b * T + t);
+    if (tok < 0 || tok >= x.rows) {
+      report(status, kStatusBadIndex);
+      tok = 0;
+    }
+  }
+  return x.ptr + (int64_t)b * x.sB + tok * x.sT + (int64_t)h * x.sH;
+}
+
+// 16-byte async copy global -> shared; src_bytes = 0 zero-fills the destination.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+               "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, FP32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 2^x with the hardware approximation (ex2.approx.ftz.f32); ex2(-inf) = +0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Row-major [rows][D] bf16 tile in shared memory with 16-byte chunks XOR-swizzled by row:
+// chunk c of row r lives at chunk (c ^ (r & 7)).  Conflict-free for ldmatrix.
+template <int D>
+__device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
+  return base + (uint32_t)(row * D * 2 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Routing rule shared by every attention kernel: is key block kb exact for (b, qb, h)?
+// proxy = (sum_d qc[d]*kc[d]) * scale with sequential FP32 sums, no FMA contraction.
+__device__ __forceinline__ bool route_selected(const AttnParams& p, const float* qbar,
+                                               const __nv_bfloat16* kcrow, float cut, int D,
+                                               int b, int qb, int kb) {
+  bool sel;
+  if (p.force == 1) {
+    sel = true;
+  } else if (p.force == 2) {
+    sel = false;
+  } else {
+    float dot = 0.f;
+    for (int d = 0; d < D; ++d)
+      dot = __fadd_rn(dot, __fmul_rn(qbar[d], __bfloat162float(kcrow[d])));
+    sel = __fmul_rn(dot, p.scale) > cut;
+  }
+  int diff = kb - qb;
+  if (diff < 0) diff = -diff;
+  sel = sel || (p.local >= 0 && diff <= p.local) || kb < p.kv_sink_blocks || qb < p.q_sink_blocks;
+  if (p.protect) sel = sel || p.protect[((int64_t)b * p.nqb + qb) * p.nkb + kb] != 0;
+  return sel;
+}
+
+}  // namespace solattn

@@ -1,0 +1,56 @@
+"""Host-side API contract (``src/sol_attn_amd/attention.py:25-91``) without a GPU."""
+
+import math
+
+import pytest
+import torch
+
+from sol_attn_b200 import dense_attention, sol_attention, sol_attention_indexed, IndexedPlan
+from sol_attn_b200 import workloads
+
+
+def test_api_rejects_unsupported_input():
+    """``tests/test_attention.py:149-156`` with the device message re-targeted to B200."""
+    q, k, v = workloads.reference_fixture()
+    with pytest.raises(ValueError, match="B200"):
+        sol_attention(q, k, v)
+    with pytest.raises(ValueError, match="Only BF16"):
+        sol_attention(q.float(), k.float(), v.float())
+    with pytest.raises(ValueError, match="Inference only"):
+        sol_attention(q.clone().requires_grad_(), k, v)
+    with pytest.raises(ValueError, match="B200"):
+        dense_attention(q, k, v)
+
+
+@pytest.mark.parametrize("shape_fix,msg", [
+    (lambda q, k, v: (q[0], k, v), "rank-4"),
+    (lambda q, k, v: (q, k[:, :10], v), "shapes must agree"),
+    (lambda q, k, v: (q[..., :32], k[..., :32], v[..., :32]), "head dimensions"),
+    (lambda q, k, v: (q.transpose(2, 3).contiguous().transpose(2, 3), k, v), "contiguous head"),
+])
+def test_api_rejects_bad_layouts(shape_fix, msg):
+    q, k, v = workloads.reference_fixture()
+    with pytest.raises(ValueError, match=msg):
+        sol_attention(*shape_fix(q, k, v))
+
+
+def test_api_rejects_masks_by_signature():
+    q, k, v = workloads.reference_fixture()
+    with pytest.raises(TypeError):
+        sol_attention(q, k, v, attn_mask=torch.ones((193, 317)))
+
+
+def test_indexed_api_validation_order():
+    q = torch.zeros((20, 2, 64), dtype=torch.bfloat16)
+    plan = IndexedPlan.create(torch.tensor([[1, 2]]), torch.arange(8).reshape(1, -1), 20)
+    with pytest.raises(ValueError, match="matching NHD"):
+        sol_attention_indexed(q, q[:10], q, plan)
+    with pytest.raises(ValueError, match="B200"):
+        sol_attention_indexed(q, q, q, plan)
+
+
+def test_sink_and_beta_validation_is_reached_only_on_device():
+    # On CPU the device check fires first, exactly like the reference's ordering.
+    q, k, v = workloads.reference_fixture()
+    with pytest.raises(ValueError):
+        sol_attention(q, k, v, beta=math.nan)

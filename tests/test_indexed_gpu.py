@@ -1,0 +1,64 @@
+"""GPU parity of sol_attention_indexed (``tests/test_indexed.py:59-88``)."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from helpers import CAbi, assert_north_star, golden, to_device
+from make_golden import indexed_cases
+from oracle import kernel_order
+from sol_attn_b200 import IndexedPlan, sol_attention_indexed
+
+pytestmark = pytest.mark.gpu
+BETAS = {"minf": -math.inf, "pinf": math.inf, "b1": 1.0}
+
+
+@pytest.mark.parametrize("tag", ["minf", "pinf", "b1"])
+def test_indexed_mask_pooling_oracle_and_unchanged_inputs(tag):
+    beta = BETAS[tag]
+    ref = golden(f"indexed_{tag}")
+    cpu, rows, keys = indexed_cases()
+    p = IndexedPlan.create(rows, keys, 1200, protected_ranges=((0, 7), (1180, 1193)), local_tokens=64)
+    gpu = [to_device(x) for x in cpu]
+    assert gpu[0].stride() == cpu[0].stride()
+    before = [x.clone() for x in gpu]
+    actual, stats = sol_attention_indexed(*gpu, p.to("cuda"), beta=beta, return_stats=True)
+    want = torch.from_numpy(ref["out"])
+    torch.testing.assert_close(actual.cpu().float(), want, atol=0.012, rtol=0.025)
+    assert (actual.cpu().float() - want).norm() / want.norm() < 0.008
+    assert_north_star(actual.cpu(), want)
+    np.testing.assert_array_equal(stats.exact_blocks.cpu().numpy(), ref["counts"])
+    if beta == -math.inf:
+        dense = F.scaled_dot_product_attention(cpu[0][rows].float().transpose(1, 2),
+                                               cpu[1][keys].float().transpose(1, 2),
+                                               cpu[2][keys].float().transpose(1, 2)).transpose(1, 2)
+        torch.testing.assert_close(actual.cpu().float(), dense, atol=0.012, rtol=0.025)
+    # Keys not in the declared mask must not affect exact OR approximate output.
+    seen = torch.unique(keys)
+    excluded = torch.ones(1200, dtype=torch.bool, device="cuda")
+    excluded[seen.to("cuda")] = False
+    gpu[1][excluded] = 80
+    gpu[2][excluded] = 80
+    assert torch.equal(actual, sol_attention_indexed(*gpu, p.to("cuda"), beta=beta))
+    assert torch.equal(gpu[0], before[0])
+    assert torch.equal(gpu[1][seen], before[1][seen])
+    assert torch.equal(gpu[2][seen], before[2][seen])
+
+
+def test_indexed_routing_and_pooling_bit_identical():
+    cpu, rows, keys = indexed_cases()
+    p = IndexedPlan.create(rows, keys, 1200, protected_ranges=((0, 7), (1180, 1193)), local_tokens=64)
+    gpu = [to_device(x) for x in cpu]
+    r = CAbi().stages(*gpu, beta=1.0, local=-1, protect=p.protected_blocks.cuda(),
+                      rows=rows.cuda(), keys=keys.cuda())
+    qg, kg, vg = cpu[0][rows], cpu[1][keys], cpu[2][keys]
+    np.testing.assert_array_equal(r["qc"].cpu().numpy(), kernel_order.pool(qg, False))
+    np.testing.assert_array_equal(r["kc"].float().cpu().numpy(), kernel_order.pool(kg, True))
+    np.testing.assert_array_equal(r["vc"].float().cpu().numpy(), kernel_order.pool(vg, True))
+    qc, kc = r["qc"].cpu().numpy(), r["kc"].float().cpu().numpy()
+    sel = kernel_order.route(qc, kc, r["cut"].cpu().numpy(), r["scale"], 0, -1, 0, 0,
+                             p.protected_blocks.numpy())
+    np.testing.assert_array_equal(r["mask"].cpu().numpy().view(np.uint32), kernel_order.pack_mask(sel))

@@ -1,0 +1,77 @@
+"""The C-ABI library loads, exports every symbol of include/solattn.h and rejects bad
+arguments on the host (no GPU needed: every rejected call returns before any CUDA call)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from sol_attn_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "solattn.h"
+
+
+def declared():
+    return re.findall(r"SOLATTN_API\s+[\w\s\*]+?\b(solattn_\w+)\s*\(", HEADER.read_text())
+
+
+def test_header_declares_the_boundary():
+    names = set(declared())
+    assert {"solattn_pool_qkv", "solattn_threshold", "solattn_attention", "solattn_sol_forward",
+            "solattn_dense", "solattn_workspace_layout", "solattn_strerror"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in declared():
+        assert hasattr(lib, name), name
+    # and the Python binding declares a signature for each of them
+    assert set(declared()) == set(_lib.SIGNATURES)
+
+
+def test_version_and_messages():
+    L = _lib.load()
+    assert b"sm_100a" in L.solattn_version()
+    for code in (0, -1, -2, -3, -4, -5):
+        assert L.solattn_strerror(code)
+
+
+def test_workspace_layout():
+    total, offs = _lib.workspace_layout(1, 32768, 32768, 24, 128)
+    nkb = nqb = 512
+    assert offs["status"] == 0
+    assert all(v % 256 == 0 for v in offs.values())
+    assert offs["vc"] - offs["kc"] >= 24 * nkb * 128 * 2
+    assert offs["mean"] - offs["qc"] >= 24 * nqb * 128 * 4
+    assert total >= offs["cutoff"] + 24 * nqb * 4
+    assert _lib.workspace_layout(1, 100, 100, 2, 96)[0] == 0      # unsupported head dim
+    assert _lib.workspace_layout(0, 100, 100, 2, 64)[0] == 0      # empty batch
+
+
+def _forward(**over):
+    args = dict(q=16, k=16, v=16, B=1, Tq=64, Tk=64, H=1, D=64, strides=(4096, 64, 64),
+                q_idx=None, kv_idx=None, idx_rows=0, protect=None, scale=0.125, beta=1.0,
+                local=1, kvs=0, qs=0, ws=256, ws_bytes=1 << 20, out=16, counts=None)
+    args.update(over)
+    a = args
+    return _lib.load().solattn_sol_forward(
+        a["q"], a["k"], a["v"], a["B"], a["Tq"], a["Tk"], a["H"], a["D"], *a["strides"],
+        *a["strides"], *a["strides"], a["q_idx"], a["kv_idx"], a["idx_rows"], a["protect"],
+        a["scale"], a["beta"], a["local"], a["kvs"], a["qs"], a["ws"], a["ws_bytes"], a["out"],
+        a["counts"], None)
+
+
+@pytest.mark.parametrize("bad,code", [
+    (dict(D=96), -2), (dict(Tq=0), -1), (dict(H=0), -1), (dict(beta=float("nan")), -1),
+    (dict(ws=None), -1), (dict(ws_bytes=16), -1), (dict(ws=128), -1), (dict(q=8), -1),
+    (dict(strides=(4096, 63, 64)), -1), (dict(q=None), -1), (dict(scale=0.0), -1),
+    (dict(scale=float("inf")), -1), (dict(kvs=-1), -1), (dict(kv_idx=16, idx_rows=0), -1),
+])
+def test_forward_rejects_bad_arguments(bad, code):
+    assert _forward(**bad) == code
+
+
+def test_threshold_rejects_nonfinite_beta():
+    L = _lib.load()
+    assert L.solattn_threshold(16, 16, 1, 1, 1, 1, 64, 0.125, float("inf"), 16, 16, 16, None) == -1
