@@ -158,9 +158,10 @@ def test_sol_matches_oracle_on_random_shapes():
         q = torch.randn((1, nq, h, d), generator=g, dtype=torch.bfloat16)
         k = torch.randn((1, nk, h, d), generator=g, dtype=torch.bfloat16)
         v = torch.randn((1, nk, h, d), generator=g, dtype=torch.bfloat16)
+        sink = min(100, nk)
         actual, stats = sol_attention(*(to_device(x) for x in (q, k, v)), beta=beta,
-                                      kv_sink_tokens=100, return_stats=True)
-        ref, counts = sol_oracle(q, k, v, beta=beta, kv_sink_tokens=100)
+                                      kv_sink_tokens=sink, return_stats=True)
+        ref, counts = sol_oracle(q, k, v, beta=beta, kv_sink_tokens=sink)
         assert_close(actual.cpu(), ref)
         assert_north_star(actual.cpu(), ref)
         assert (stats.exact_blocks.cpu() - counts).abs().sum() <= 2
