@@ -4,8 +4,9 @@
  *
  * Every entry point takes raw device pointers, sizes, element strides, scalars and a
  * CUDA stream passed as `void*` (a cudaStream_t; NULL is the legacy default stream). No
- * entry point allocates, synchronises or keeps state between calls: buffers are owned by
- * the caller (in the Python layer, torch). Work is enqueued on `stream` asynchronously.
+ * entry point allocates or synchronises (solattn_read_status excepted): buffers are owned by
+ * the caller (in the Python layer, torch), and only solattn_sol_forward_noalloc keeps state
+ * between calls (its fixed scratch array). Work is enqueued on `stream` asynchronously.
  * Return value: SOLATTN_OK (0) or a negative SOLATTN_ERR_* code; solattn_strerror() gives
  * the message. Errors that a kernel detects on the device (a bounded wait that ran out, an
  * index outside its tensor) are written to the caller's status word (see
@@ -43,6 +44,7 @@ extern "C" {
 #define SOLATTN_ERR_LAUNCH (-3)      /* CUDA reported an error at launch */
 #define SOLATTN_ERR_DEVICE (-4)      /* a kernel reported a device-side error in the status word */
 #define SOLATTN_ERR_CUDA (-5)        /* a CUDA runtime call failed */
+#define SOLATTN_ERR_TOO_LARGE (-6)   /* the problem needs more scratch than the fixed no-allocation array */
 
 /* Routing force modes (kernels.py:208): 0 threshold, 1 all blocks exact (beta=-inf),
  * 2 only protected blocks exact (beta=+inf). */
@@ -151,6 +153,36 @@ SOLATTN_API int solattn_dense(const void* q, const void* k, const void* v,
                   int64_t k_sB, int64_t k_sT, int64_t k_sH,
                   int64_t v_sB, int64_t v_sT, int64_t v_sH,
                   float scale, void* out, void* stream);
+
+/*
+ * All-in SOL forward that allocates nothing (no counterpart in the reference).
+ * For callers that cannot allocate device memory at call time - e.g. a plugin inside a host
+ * program that owns all device memory through its own pool and forbids direct cudaMalloc, or a
+ * latency-critical loop that cannot afford cudaMalloc's implicit synchronisation.  Same
+ * arguments and results as solattn_sol_forward minus the workspace: the scratch is a fixed
+ * file-scope device array of solattn_noalloc_scratch_bytes() bytes (16 MiB) that every GPU
+ * loading this library holds until the process exits.  Problems whose
+ * solattn_workspace_layout() size exceeds it return SOLATTN_ERR_TOO_LARGE before any GPU work.
+ * All calls on a device share that array and it keeps the last call's contents (the status
+ * word is cleared by each call; everything else a call reads, it writes first), so calls that
+ * overlap on the GPU - different streams without ordering, or concurrent host threads - race.
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress with
+ * that device current) and caches it; make that first call before any stream capture begins.
+ * Calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+SOLATTN_API int solattn_sol_forward_noalloc(const void* q, const void* k, const void* v,
+                        int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                        int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                        int64_t k_sB, int64_t k_sT, int64_t k_sH,
+                        int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                        const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                        const uint8_t* protect,
+                        float scale, float beta, int local, int kv_sink_blocks,
+                        int q_sink_blocks, void* out, int32_t* counts, void* stream);
+
+/* Size in bytes of the fixed scratch array used by solattn_sol_forward_noalloc (no counterpart
+ * in the reference). */
+SOLATTN_API int64_t solattn_noalloc_scratch_bytes(void);
 
 /*
  * Synchronises `stream`, copies the device status word at `status` to the host, clears it

@@ -98,6 +98,7 @@ const char* solattn_strerror(int code) {
     case SOLATTN_ERR_LAUNCH: return "kernel launch failed";
     case SOLATTN_ERR_DEVICE: return "device-side error reported by a kernel";
     case SOLATTN_ERR_CUDA: return "CUDA runtime call failed";
+    case SOLATTN_ERR_TOO_LARGE: return "problem exceeds the fixed no-allocation scratch array";
     default: return "unknown error";
   }
 }

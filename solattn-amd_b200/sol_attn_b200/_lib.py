@@ -31,6 +31,10 @@ SIGNATURES = {
                             + [c_float, c_float, c_int, c_int, c_int, _P, _I64, _P, _P, _P]),
     "solattn_dense": (c_int, [_P, _P, _P] + [_I64] * 5 + [_I64] * 9 + [c_float, _P, _P]),
     "solattn_read_status": (c_int, [_P, _P, _P]),
+    "solattn_sol_forward_noalloc": (c_int, [_P, _P, _P] + [_I64] * 5 + [_I64] * 9
+                                    + [_P, _P, _I64, _P]
+                                    + [c_float, c_float, c_int, c_int, c_int, _P, _P, _P]),
+    "solattn_noalloc_scratch_bytes": (_I64, []),
 }
 
 _lib = None
