@@ -114,11 +114,6 @@ def make_inputs():
     return workloads.video_dit(b=B, t=T, h=H, d=D, sigma=0.3, seed=0)
 
 
-def shard(rank, world):
-    per = H // world
-    return rank * per, (rank + 1) * per
-
-
 def time_cpu_oracle(qh, kh, vh, n_qblocks, threads, heads=(0,)):
     """Oracle port on ``heads`` and ``n_qblocks`` evenly spaced q-blocks of each; the time is
     extrapolated linearly to the whole call (all heads, all q-blocks).
@@ -207,7 +202,8 @@ def main():
     from sol_attn_b200.stages import Stages
 
     qh, kh, vh = make_inputs()
-    h0, h1 = shard(rank, world)
+    from sol_attn_b200.sharding import head_shard
+    h0, h1 = head_shard(H, rank, world)
     qd, kd, vd = (x.to(dev) for x in (qh, kh, vh))
     q, k, v = (x[:, :, h0:h1] for x in (qd, kd, vd))  # strided head shard, no copy
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
@@ -290,16 +286,10 @@ def main():
     d2h = hout.numel() * hout.element_size()
 
     # ---------------- reduce over ranks (after timing) ----------------
-    vals = torch.tensor([ms, e2e_ms, k_ms["pool"], k_ms["threshold"], k_ms["attention"]],
-                        dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-        gathered = [torch.empty_like(counts) for _ in range(world)]
-        dist.all_gather(gathered, counts)
-        counts_all = torch.cat(gathered, dim=2)
-    else:
-        counts_all = counts
-    ms, e2e_ms, pool_ms, thr_ms, attn_ms = vals.tolist()
+    from sol_attn_b200.sharding import gather_heads, max_over_ranks
+    ms, e2e_ms, pool_ms, thr_ms, attn_ms = max_over_ranks(
+        [ms, e2e_ms, k_ms["pool"], k_ms["threshold"], k_ms["attention"]], device=dev)
+    counts_all = gather_heads(counts, head_dim=2)
 
     nkb = nqb = T // 64
     total_exact = int(counts_all.sum())
