@@ -15,8 +15,9 @@ bit identity:
   mean = s1/n, var = max(s2/n - mean*mean, 0);
 * cutoff: sequential sums over d of qc*mean and (qc*qc)*var,
   cutoff = (mu + beta*sqrt(sg)) * scale;
-* routing (fused kernel prologue): proxy = (sequential sum over d of qc*kc) * scale,
-  exact iff proxy > cutoff (force modes and the local / sink / protected rules as in
+* routing (fused kernel prologue): proxy = dot * scale where dot sums qc*kc as eight
+  partial sums p_j over d = 8i + j (i increasing) combined as
+  ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); exact iff proxy > cutoff (force modes and the local / sink / protected rules as in
   ``reference.py:41-51``).
 
 Routing decisions computed here from the GPU's own pooled statistics must equal the GPU's
@@ -90,9 +91,12 @@ def route(qc, kc, cutoff, scale, force, local, kv_sink_blocks, q_sink_blocks, pr
     elif force == 2:
         sel = np.zeros((B, H, nqb, nkb), bool)
     else:
-        dot = np.zeros((B, H, nqb, nkb), F32)
-        for d in range(D):
-            dot = dot + qc[:, :, :, None, d] * kc[:, :, None, :, d]
+        part = [np.zeros((B, H, nqb, nkb), F32) for _ in range(8)]
+        for i in range(D // 8):
+            for j in range(8):
+                d = 8 * i + j
+                part[j] = part[j] + qc[:, :, :, None, d] * kc[:, :, None, :, d]
+        dot = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]))
         sel = (dot * F32(scale)) > cutoff[..., None]
     qb = np.arange(nqb)[:, None]
     kb = np.arange(nkb)[None, :]

@@ -15,6 +15,7 @@ constexpr int kBlock = 64;  // tokens per routing block (kernels.py:12)
 constexpr int kStatusWaitTimeout = 1;  // a bounded mbarrier wait ran out
 constexpr int kStatusBadIndex = 2;     // a gather index outside its tensor
 constexpr int kStatusTmem = 3;         // TMEM allocation returned an unusable address
+constexpr int kStatusBadTma = 4;       // a TMA tile coordinate outside its tensor (load skipped)
 
 struct TensorView {
   const __nv_bfloat16* ptr;
@@ -125,8 +126,31 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
   return base + (uint32_t)(row * D * 2 + ((chunk ^ (row & 7)) << 4));
 }
 
+// Routing proxy dot product sum_d qbar[d] * kc[d] in a fixed order shared by every kernel and
+// by its CPU restatement: eight partial sums p_j over d = 8i + j (i increasing), each product
+// and sum rounded to nearest FP32 (no FMA contraction), then
+// ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).  kcrow must be 16-byte aligned.
+__device__ __forceinline__ float routing_dot(const float* qbar, const __nv_bfloat16* kcrow, int D) {
+  float p[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) p[j] = 0.f;
+  for (int i = 0; i < D / 8; ++i) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(kcrow) + i);
+    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 kf = __bfloat1622float2(k2[j]);
+      p[2 * j] = __fadd_rn(p[2 * j], __fmul_rn(qbar[8 * i + 2 * j], kf.x));
+      p[2 * j + 1] = __fadd_rn(p[2 * j + 1], __fmul_rn(qbar[8 * i + 2 * j + 1], kf.y));
+    }
+  }
+  return __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])),
+                   __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+}
+
 // Routing rule shared by every attention kernel: is key block kb exact for (b, qb, h)?
-// proxy = (sum_d qc[d]*kc[d]) * scale with sequential FP32 sums, no FMA contraction.
+// Threshold mode: (routing_dot * scale) > cut.  Then the force modes and the local / sink /
+// protected rules of reference.py:41-51 (kernels.py:136-143).
 __device__ __forceinline__ bool route_selected(const AttnParams& p, const float* qbar,
                                                const __nv_bfloat16* kcrow, float cut, int D,
                                                int b, int qb, int kb) {
@@ -136,10 +160,7 @@ __device__ __forceinline__ bool route_selected(const AttnParams& p, const float*
   } else if (p.force == 2) {
     sel = false;
   } else {
-    float dot = 0.f;
-    for (int d = 0; d < D; ++d)
-      dot = __fadd_rn(dot, __fmul_rn(qbar[d], __bfloat162float(kcrow[d])));
-    sel = __fmul_rn(dot, p.scale) > cut;
+    sel = __fmul_rn(routing_dot(qbar, kcrow, D), p.scale) > cut;
   }
   int diff = kb - qb;
   if (diff < 0) diff = -diff;
