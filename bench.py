@@ -179,6 +179,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--heads", type=int, default=H,
+                    help="profiling only: run the first HEADS heads of the workload")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -188,8 +191,9 @@ def main():
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if H % world:
-        raise SystemExit(f"{H} heads do not shard over {world} ranks")
+    heads = args.heads
+    if heads % world or not 0 < heads <= H:
+        raise SystemExit(f"{heads} heads do not shard over {world} ranks")
 
     import torch.distributed as dist
     from datetime import timedelta
@@ -203,7 +207,7 @@ def main():
 
     qh, kh, vh = make_inputs()
     from sol_attn_b200.sharding import head_shard
-    h0, h1 = head_shard(H, rank, world)
+    h0, h1 = head_shard(heads, rank, world)
     qd, kd, vd = (x.to(dev) for x in (qh, kh, vh))
     q, k, v = (x[:, :, h0:h1] for x in (qd, kd, vd))  # strided head shard, no copy
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
@@ -258,32 +262,34 @@ def main():
     counts = st.counts.clone()
 
     # ---------------- end-to-end from pinned host buffers ----------------
-    hq, hk, hv = (x[:, :, h0:h1].contiguous().pin_memory() for x in (qh, kh, vh))
-    hout = torch.empty((B, T, h1 - h0, D), dtype=torch.bfloat16).pin_memory()
-    dq, dk, dv = (torch.empty_like(x, device=dev) for x in (hq, hk, hv))
-    e2e_steps = max(3, args.steps // 2)
+    e2e_ms, h2d, d2h = float("nan"), 0, 0
+    if not args.no_e2e:
+        hq, hk, hv = (x[:, :, h0:h1].contiguous().pin_memory() for x in (qh, kh, vh))
+        hout = torch.empty((B, T, h1 - h0, D), dtype=torch.bfloat16).pin_memory()
+        dq, dk, dv = (torch.empty_like(x, device=dev) for x in (hq, hk, hv))
+        e2e_steps = max(3, args.steps // 2)
 
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        out = sol_attention(dq, dk, dv, **kw)
-        hout.copy_(out, non_blocking=True)
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            out = sol_attention(dq, dk, dv, **kw)
+            hout.copy_(out, non_blocking=True)
 
-    for _ in range(3):
-        e2e_step()
-    barrier()
-    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(e2e_steps)]
-    for s, e in e2e_ev:
-        flush.zero_()
-        s.record()
-        e2e_step()
-        e.record()
-    barrier()
-    e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in e2e_ev)
-    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
-    d2h = hout.numel() * hout.element_size()
+        for _ in range(3):
+            e2e_step()
+        barrier()
+        e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(e2e_steps)]
+        for s, e in e2e_ev:
+            flush.zero_()
+            s.record()
+            e2e_step()
+            e.record()
+        barrier()
+        e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in e2e_ev)
+        h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+        d2h = hout.numel() * hout.element_size()
 
     # ---------------- reduce over ranks (after timing) ----------------
     from sol_attn_b200.sharding import gather_heads, max_over_ranks
@@ -293,7 +299,8 @@ def main():
 
     nkb = nqb = T // 64
     total_exact = int(counts_all.sum())
-    density = total_exact / (B * H * nqb * nkb)
+    density = total_exact / (B * heads * nqb * nkb)
+    dense_flops = DENSE_FLOPS * heads / H
     # Algorithmic FLOPs of the fused kernel on this rank's shard: every selected block is a
     # 64x64 exact tile (T is a multiple of 64), every unselected block one centroid column.
     my_exact = int(counts.sum())
@@ -324,11 +331,12 @@ def main():
                "rel_l2": float((got[:, rows] - ref[:, rows]).norm() / ref[:, rows].norm()),
                "vs": "CPU oracle, head 0, sampled q-blocks", "q_blocks": len(blocks)}
         result = {
-            "metric": METRIC, "value": DENSE_FLOPS / (ms * 1e-3) / 1e12, "unit": UNIT,
+            "metric": METRIC, "value": dense_flops / (ms * 1e-3) / 1e12, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded block-smooth drift inputs, no captured activations)",
-            "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "heads": H,
+            "config": {"workload": WORKLOAD if heads == H else f"{WORKLOAD} (first {heads} heads)",
+                       "global_batch": B, "seq_len": T, "heads": heads,
                        "head_dim": D, "parallelism": f"head-sharded x{world}",
                        "l2": "flushed between timed steps (256 MiB write), inputs 604 MB"},
             "density": density, "err": err,
@@ -341,7 +349,7 @@ def main():
                               "unit": "GB/s", "frac": pool_gbs / pk["hbm_gbs"],
                               "bytes_per_launch": pool_bytes, "peak_source": pk_kind},
             "cpu_baseline": cpu,
-            "e2e": {"value": DENSE_FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+            "e2e": {"value": dense_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                     "ms_per_call": e2e_ms, "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "gpu_launches": st.launches() * args.steps * world,

@@ -139,9 +139,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + L::kMask);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x;
+  // Query tiles of one head are adjacent in launch order so that the CTAs resident at any time
+  // share that head's K/V (16 MB at T=32k) in L2.
+  const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
-  const int qb0 = 2 * blockIdx.y;
+  const int qb0 = 2 * blockIdx.x;
   const bool has1 = qb0 + 1 < p.nqb;
   const int nwords = (p.nkb + 31) / 32;
   int* sTiles = reinterpret_cast<int*>(smem + L::tiles_offset(nwords));
@@ -157,7 +159,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     misc[2] = 0;
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(smem_u32(misc), kTmemCols);
+  if (warp == 0) {
+    tmem_alloc(smem_u32(misc), kTmemCols);
+    // Give up the allocation permit at once: while a CTA holds it, no further CTA that needs
+    // TMEM is launched on this SM, and two CTAs per SM are what hides the softmax.
+    tmem_relinquish();
+  }
   if (p.force == 0) {
     for (int i = tid; i < 2 * D; i += kThreads) {
       const int qb = qb0 + i / D;
@@ -180,23 +187,32 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_load_4d(sQ + j * kBoxBytes, &tmQ, bar0 + 8 * Q_FULL, 64 * j, qb0 * kBlock, h, b);
   }
 
-  // ---- routing of both q-blocks into shared bitmasks (one ballot per 32 key blocks) ----
+  // ---- routing of both q-blocks into shared bitmasks ----
+  // Lane kb of a warp reads centroid row kb once and forms both q-blocks' proxies from it (the
+  // arithmetic of common.cuh:route_selected, bit for bit); one ballot per q-block per 32 blocks.
   const __nv_bfloat16* kc_bh = p.kc + (int64_t)bh * p.nkb * D;
-  for (int w = warp; w < 2 * nwords; w += kThreads / 32) {
-    const int qsel = w / nwords, wi = w % nwords;
-    const int qb = qb0 + qsel;
+  for (int wi = warp; wi < nwords; wi += kThreads / 32) {
     const int kb = wi * 32 + lane;
-    const int qbc = qb < p.nqb ? qb : p.nqb - 1;  // clamped: every address stays in range
-    const int kbc = kb < p.nkb ? kb : p.nkb - 1;
-    bool sel = false;
-    if (kb < p.nkb && qb < p.nqb) {
-      const float cut = p.force == 0 ? p.cutoff[(int64_t)bh * p.nqb + qbc] : 0.f;
-      sel = route_selected(p, sQbar + qsel * D, kc_bh + (int64_t)kbc * D, cut, D, b, qbc, kbc);
+    const int kbc = kb < p.nkb ? kb : p.nkb - 1;  // clamped: every address stays in range
+    bool sel[2] = {false, false};
+    if (p.force == 0) {
+      float d0, d1;
+      routing_dot2(sQbar, sQbar + D, kc_bh + (int64_t)kbc * D, D, d0, d1);
+      const float cut0 = p.cutoff[(int64_t)bh * p.nqb + qb0];
+      const float cut1 = has1 ? p.cutoff[(int64_t)bh * p.nqb + qb0 + 1] : 0.f;
+      sel[0] = __fmul_rn(d0, p.scale) > cut0;
+      sel[1] = __fmul_rn(d1, p.scale) > cut1;
     }
-    const uint32_t bal = __ballot_sync(0xffffffffu, sel);
-    if (lane == 0) {
-      sMask[qsel * nwords + wi] = bal;
-      if (p.debug_mask && qb < p.nqb) p.debug_mask[((int64_t)bh * p.nqb + qb) * nwords + wi] = bal;
+#pragma unroll
+    for (int qsel = 0; qsel < 2; ++qsel) {
+      const int qb = qb0 + qsel;
+      bool s_ = false;
+      if (kb < p.nkb && qb < p.nqb) s_ = route_rules(p, sel[qsel], b, qb, kb);
+      const uint32_t bal = __ballot_sync(0xffffffffu, s_);
+      if (lane == 0) {
+        sMask[qsel * nwords + wi] = bal;
+        if (p.debug_mask && qb < p.nqb) p.debug_mask[((int64_t)bh * p.nqb + qb) * nwords + wi] = bal;
+      }
     }
   }
   __syncthreads();
@@ -456,7 +472,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_relinquish();
     tmem_dealloc(tmem, kTmemCols);
   }
 }
@@ -523,7 +538,7 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
   cudaError_t err = cudaFuncSetAttribute(attn_sm100_kernel<D>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  dim3 grid(p.B * p.H, (p.nqb + 1) / 2);
+  dim3 grid((p.nqb + 1) / 2, p.B * p.H);
   attn_sm100_kernel<D><<<grid, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
   return cudaGetLastError();
 }

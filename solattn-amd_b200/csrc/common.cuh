@@ -148,6 +148,44 @@ __device__ __forceinline__ float routing_dot(const float* qbar, const __nv_bfloa
                    __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
 }
 
+// Two routing dots against one centroid row (same order and rounding as routing_dot).
+__device__ __forceinline__ void routing_dot2(const float* qa, const float* qb,
+                                             const __nv_bfloat16* kcrow, int D, float& da,
+                                             float& db) {
+  float pa[8], pb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) pa[j] = pb[j] = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < D / 8; ++i) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(kcrow) + i);
+    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 kf = __bfloat1622float2(k2[j]);
+      pa[2 * j] = __fadd_rn(pa[2 * j], __fmul_rn(qa[8 * i + 2 * j], kf.x));
+      pa[2 * j + 1] = __fadd_rn(pa[2 * j + 1], __fmul_rn(qa[8 * i + 2 * j + 1], kf.y));
+      pb[2 * j] = __fadd_rn(pb[2 * j], __fmul_rn(qb[8 * i + 2 * j], kf.x));
+      pb[2 * j + 1] = __fadd_rn(pb[2 * j + 1], __fmul_rn(qb[8 * i + 2 * j + 1], kf.y));
+    }
+  }
+  da = __fadd_rn(__fadd_rn(__fadd_rn(pa[0], pa[1]), __fadd_rn(pa[2], pa[3])),
+                 __fadd_rn(__fadd_rn(pa[4], pa[5]), __fadd_rn(pa[6], pa[7])));
+  db = __fadd_rn(__fadd_rn(__fadd_rn(pb[0], pb[1]), __fadd_rn(pb[2], pb[3])),
+                 __fadd_rn(__fadd_rn(pb[4], pb[5]), __fadd_rn(pb[6], pb[7])));
+}
+
+// The force modes and the local / sink / protected rules (reference.py:41-51,
+// kernels.py:136-143) applied to a threshold decision `sel`.
+__device__ __forceinline__ bool route_rules(const AttnParams& p, bool sel, int b, int qb, int kb) {
+  if (p.force == 1) sel = true;
+  if (p.force == 2) sel = false;
+  int diff = kb - qb;
+  if (diff < 0) diff = -diff;
+  sel = sel || (p.local >= 0 && diff <= p.local) || kb < p.kv_sink_blocks || qb < p.q_sink_blocks;
+  if (p.protect) sel = sel || p.protect[((int64_t)b * p.nqb + qb) * p.nkb + kb] != 0;
+  return sel;
+}
+
 // Routing rule shared by every attention kernel: is key block kb exact for (b, qb, h)?
 // Threshold mode: (routing_dot * scale) > cut.  Then the force modes and the local / sink /
 // protected rules of reference.py:41-51 (kernels.py:136-143).
