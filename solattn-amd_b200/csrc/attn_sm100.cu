@@ -1,27 +1,23 @@
 // Fused routed attention on the Blackwell data path (replaces `_sol`, kernels.py:101-182).
 //
-// One CTA = one 128-row query tile = two 64-row q-blocks (qb0 = 2*y, qb0 + 1) of one (b, h),
-// 128 threads, two CTAs per SM (256 TMEM columns and ~104 KB of shared memory each) so that one
-// CTA's softmax overlaps the other CTA's tensor-core work.
+// One CTA = one 128-row query tile = two 64-row q-blocks (qb0 = 2*x, qb0 + 1) of one (b, h);
+// 160 threads, two CTAs per SM (256 TMEM columns and ~100 KB of shared memory each).
 //
-// Per CTA:
-//   1. Prologue: TMEM allocation (warp 0), routing of every key block for both q-blocks into
-//      shared bitmasks (common.cuh:route_selected, bit-identical to the CPU restatement), and a
-//      tile list in shared memory built by warp 0:
-//        - centroid tiles (128 pooled keys kc/vc) holding a block unselected by either q-block:
-//          entry -(t + 1);
-//        - exact tiles: the union of both q-blocks' exact blocks, two blocks per tile in
-//          increasing order: entry a | (b << 16), b = kNoBlock (0x7FFF) when the tile has one
-//          block.  Every exact entry is non-negative (block ids < kMaxKeyBlocks < 0x7FFF), so
-//          the sign alone tells the two kinds apart.
-//   2. Tile loop, all four warps in lockstep (warp w owns TMEM lanes / rows 32w..32w+31),
-//      thread 0 issuing TMA and tcgen05.mma:
-//        S = Q K^T  (SMEM x SMEM -> TMEM, FP32)      -> S_FULL
-//        next K tile TMA (the S MMA has released the K buffer)
-//        softmax per row: column mask/bias for the row's q-block, FP32 online softmax with lazy
-//        rescaling, P (BF16) written over S in TMEM
-//        O += P V  (TMEM x SMEM -> TMEM)               -> O_DONE, then the next V tile TMA
-//   3. Epilogue O / l -> BF16 global stores; TMEM released.
+// Tiles hold 64 keys: one exact key block, or 64 pooled centroids.  The tile list (shared
+// memory, built by warp 0 after routing) holds first every 64-centroid group that still has a
+// block unselected by either q-block (entry -(t + 1)), then every block of the union of both
+// q-blocks' exact sets in increasing order (entry kb >= 0).  A row whose q-block did not select
+// an exact block sees it as -inf; a centroid whose block is exact for the row's q-block too.
+//
+// Warp roles:
+//   warps 0-3  softmax: warp w owns TMEM lanes / tile rows 32w..32w+31.  Per tile: wait S_FULL,
+//              tcgen05.ld S, mask/bias, FP32 online softmax with lazy rescaling, P (BF16) written
+//              over its S buffer, arrive P_FULL.  Epilogue O / l -> BF16.
+//   warp 4     TMA + MMA issue (lane 0): Q once; K and V through 2-slot rings; for tile i it
+//              issues S_i = Q K_i^T into TMEM buffer i%2, then O += P_{i-1} V_{i-1}, so the
+//              tensor core works on S_{i+1} and P V while the softmax warps work on tile i.
+// TMEM: S buffers at columns [0, 64) and [64, 128) (P packed into the first 32 columns of its
+// buffer), O at [128, 128 + D).
 #include <cudaTypedefs.h>
 
 #include "sm100.cuh"
@@ -32,31 +28,39 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kRows = 128;     // query rows per CTA
-constexpr int kKeys = 128;     // keys per tile
-constexpr int kThreads = 128;  // 4 warps
+constexpr int kRows = 128;         // query rows per CTA
+constexpr int kKeys = 64;          // keys per tile
+constexpr int kSoftmaxWarps = 4;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 1);
 constexpr uint32_t kTmemCols = 256;
-constexpr int kBoxBytes = kRows * 128;  // one 128-row x 64-column BF16 box (16 KB)
-constexpr int kMaxKeyBlocks = 4096;     // tile list capacity (T <= 262144 keys)
-constexpr int kNoBlock = 0x7FFF;        // second half of a one-block exact tile
+constexpr int kQBox = kRows * 128;   // one 128-row x 64-column BF16 box of Q (16 KB)
+constexpr int kKVBox = kKeys * 128;  // one 64-row x 64-column BF16 box of K or V (8 KB)
+constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
 
-enum Bar { Q_FULL, K_FULL, V_FULL, S_FULL, O_DONE, DRAIN, NBARS };
+// Barriers: slot-indexed pairs for the 2-deep rings.
+enum Bar {
+  Q_FULL,
+  K_FULL0, K_FULL1, V_FULL0, V_FULL1,
+  S_FULL0, S_FULL1, P_FULL0, P_FULL1, PV_DONE0, PV_DONE1,
+  DRAIN, NBARS
+};
 
 template <int D>
 struct Layout {
-  static constexpr int kTile = kRows * D * 2;  // bytes of a 128 x D BF16 tile
+  static constexpr int kQTile = kRows * D * 2;   // 128 x D BF16
+  static constexpr int kKVTile = kKeys * D * 2;  // 64 x D BF16
   static constexpr int kQ = 0;
-  static constexpr int kK = kTile;
-  static constexpr int kV = 2 * kTile;
-  static constexpr int kBars = 3 * kTile;
-  static constexpr int kMisc = kBars + NBARS * 8;  // [0] TMEM address [1] abort [2] tiles
-  static constexpr int kQbar = kMisc + 16;         // float [2][D]
-  static constexpr int kMask = kQbar + 2 * D * 4;  // uint32 [2][nwords]
-  __host__ __device__ static int tiles_offset(int nwords) { return kMask + 2 * nwords * 4; }
-  __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + (nkb + 1) / 2; }
+  static constexpr int kK = kQTile;                 // 2 slots
+  static constexpr int kV = kK + 2 * kKVTile;       // 2 slots
+  static constexpr int kBars = kV + 2 * kKVTile;
+  static constexpr int kMisc = kBars + NBARS * 8;   // [0] TMEM address [1] abort [2] tiles
+  static constexpr int kQbar = kMisc + 16;          // float [2][D]
+  static constexpr int kMask = kQbar + 2 * D * 4;   // uint32 [2][nwords]
+  __host__ __device__ static int tiles_offset(int nwords) { return kMask + 2 * nwords * 4; }  // int16
+  __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + nkb; }
   static size_t bytes(int nkb) {
     const int nwords = (nkb + 31) / 32;
-    size_t n = 1024 + (size_t)tiles_offset(nwords) + (size_t)max_tiles(nkb) * 4;
+    size_t n = 1024 + (size_t)tiles_offset(nwords) + (size_t)max_tiles(nkb) * 2;
     // At most two CTAs per SM: each holds 256 of the SM's 512 TMEM columns.
     return n < 80 * 1024 ? 80 * 1024 : n;
   }
@@ -77,40 +81,6 @@ __device__ __forceinline__ void mbar_wait_quiet(uint32_t bar, uint32_t parity) {
   }
 }
 
-}  // namespace
-
-namespace {
-
-// Issues the TMA loads of one K or V tile (tile-list entry `e`) into `dst` on barrier `full`.
-// Centroid tiles read 128 pooled rows as two 64-row boxes (a second half starting past the
-// last centroid repeats the first; its columns are masked).  Exact tiles read two 64-key blocks
-// (a one-block tile repeats its block; the repeat is masked).  All rows are inside the tensors.
-static_assert(kMaxKeyBlocks < kNoBlock, "block ids must stay below the one-block sentinel");
-template <int D>
-__device__ __forceinline__ void load_kv_tile(uint32_t dst, const CUtensorMap* tile_map,
-                                             const CUtensorMap* cent_map, uint32_t full, int e,
-                                             int nkb, int h, int b) {
-  mbar_expect_tx(full, (uint32_t)(kKeys * D * 2));
-  if (e < 0) {
-    const int c0 = kKeys * (-e - 1);
-    const int c1 = c0 + kBlock < nkb ? c0 + kBlock : c0;
-#pragma unroll
-    for (int j = 0; j < D / 64; ++j) {
-      tma_load_4d(dst + j * kBoxBytes, cent_map, full, 64 * j, c0, h, b);
-      tma_load_4d(dst + j * kBoxBytes + kBlock * 128, cent_map, full, 64 * j, c1, h, b);
-    }
-  } else {
-    const int a = e & 0xffff;
-    const int hi = (e >> 16) & 0xffff;
-    const int bb = hi == kNoBlock ? a : hi;
-#pragma unroll
-    for (int j = 0; j < D / 64; ++j) {
-      tma_load_4d(dst + j * kBoxBytes, tile_map, full, 64 * j, kBlock * a, h, b);
-      tma_load_4d(dst + j * kBoxBytes + kBlock * 128, tile_map, full, 64 * j, kBlock * bb, h, b);
-    }
-  }
-}
-
 // Every lane waits; the warp agrees on the outcome (false after a timeout or an abort).
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int32_t* status) {
@@ -118,7 +88,23 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok);
 }
 
+// TMA loads of one K or V tile (tile-list entry e) into `dst` on barrier `full`: 64 centroid rows
+// of the pooled map (e < 0) or the 64 rows of key block e.  Rows past the end of a tensor are
+// filled with zeros by the TMA unit and masked by the softmax.
+template <int D>
+__device__ __forceinline__ void load_kv_tile(uint32_t dst, const CUtensorMap* tile_map,
+                                             const CUtensorMap* cent_map, uint32_t full, int e,
+                                             int h, int b) {
+  mbar_expect_tx(full, (uint32_t)(kKeys * D * 2));
+  const bool cent = e < 0;
+  const int row = cent ? kKeys * (-e - 1) : kBlock * e;
+#pragma unroll
+  for (int j = 0; j < D / 64; ++j)
+    tma_load_4d(dst + j * kKVBox, cent ? cent_map : tile_map, full, 64 * j, row, h, b);
+}
+
 }  // namespace
+
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -133,6 +119,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sQ = sbase + L::kQ, sK = sbase + L::kK, sV = sbase + L::kV;
   const uint32_t bar0 = sbase + L::kBars;
+  auto bar = [bar0](int i) { return bar0 + 8u * (uint32_t)i; };
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   float* sQbar = reinterpret_cast<float*>(smem + L::kQbar);
@@ -146,15 +133,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int qb0 = 2 * blockIdx.x;
   const bool has1 = qb0 + 1 < p.nqb;
   const int nwords = (p.nkb + 31) / 32;
-  int* sTiles = reinterpret_cast<int*>(smem + L::tiles_offset(nwords));
+  int16_t* sTiles = reinterpret_cast<int16_t*>(smem + L::tiles_offset(nwords));
 
   if (tid == 0) {
-    mbar_init(bar0 + 8 * Q_FULL, 1);
-    mbar_init(bar0 + 8 * K_FULL, 1);
-    mbar_init(bar0 + 8 * V_FULL, 1);
-    mbar_init(bar0 + 8 * S_FULL, 1);
-    mbar_init(bar0 + 8 * O_DONE, 1);
-    mbar_init(bar0 + 8 * DRAIN, 1);
+    for (int i = 0; i < NBARS; ++i)
+      mbar_init(bar(i), (i == P_FULL0 || i == P_FULL1) ? kSoftmaxWarps : 1);
     misc[1] = 0;
     misc[2] = 0;
     mbar_fence_init();
@@ -176,15 +159,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (tid == 0) {
+  if (tid == kSoftmaxWarps * 32) {  // the TMA/MMA thread starts Q early
     tma_prefetch(&tmQ);
     tma_prefetch(&tmK);
     tma_prefetch(&tmV);
     tma_prefetch(&tmKC);
     tma_prefetch(&tmVC);
-    mbar_expect_tx(bar0 + 8 * Q_FULL, L::kTile);
+    mbar_expect_tx(bar(Q_FULL), L::kQTile);
     for (int j = 0; j < D / 64; ++j)
-      tma_load_4d(sQ + j * kBoxBytes, &tmQ, bar0 + 8 * Q_FULL, 64 * j, qb0 * kBlock, h, b);
+      tma_load_4d(sQ + j * kQBox, &tmQ, bar(Q_FULL), 64 * j, qb0 * kBlock, h, b);
   }
 
   // ---- routing of both q-blocks into shared bitmasks ----
@@ -227,19 +210,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int t = t0 + lane;
       bool useful = false;
       if (t < nct) {
-        for (int wi = 4 * t; wi < 4 * t + 4 && wi < nwords; ++wi) {
+        for (int wi = 2 * t; wi < 2 * t + 2 && wi < nwords; ++wi) {
           const uint32_t v = valid_word(wi, p.nkb);
           const uint32_t w0 = m0[wi], w1 = m1[wi];
           if ((~w0 & v) || (has1 && (~w1 & v))) useful = true;
         }
       }
       const uint32_t bal = __ballot_sync(0xffffffffu, useful);
-      if (useful) sTiles[n + __popc(bal & ((1u << lane) - 1u))] = -(t + 1);
+      if (useful) sTiles[n + __popc(bal & ((1u << lane) - 1u))] = (int16_t)(-(t + 1));
       n += __popc(bal);
     }
-    // Exact blocks of the union in increasing order; block of rank r goes to the low (r even)
-    // or high (r odd) 16 bits of entry n + r/2.
-    uint16_t* half = reinterpret_cast<uint16_t*>(sTiles + n);
     int r = 0;
     for (int w0 = 0; w0 < nwords; w0 += 32) {
       const int wi = w0 + lane;
@@ -252,19 +232,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
       }
-      int rank = r + incl - cnt;
+      int rank = n + r + incl - cnt;
       while (bits) {
         const int bit = __ffs(bits) - 1;
         bits &= bits - 1u;
-        half[rank++] = (uint16_t)(32 * wi + bit);
+        sTiles[rank++] = (int16_t)(32 * wi + bit);
       }
       r += __shfl_sync(0xffffffffu, incl, 31);
     }
-    __syncwarp();
-    if (lane == 0) {
-      if (r & 1) half[r] = (uint16_t)kNoBlock;  // one-block last tile
-      misc[2] = (uint32_t)(n + (r + 1) / 2);
-    }
+    if (lane == 0) misc[2] = (uint32_t)(n + r);
     if (lane < 2 && p.counts && qb0 + lane < p.nqb) {
       int c = 0;
       for (int i = 0; i < nwords; ++i) c += __popc(sMask[lane * nwords + i]);
@@ -274,107 +250,161 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   const int ntiles = (int)misc[2];
 
-  // ---- tile loop ----
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;  // warp w reads TMEM lanes 32w..32w+31
-  const uint32_t tS = tmem, tO = tmem + kKeys;
-  const uint32_t tSr = tS + lane_base, tOr = tO + lane_base;
-  const int row = warp * 32 + lane;
-  const int qsel = row >> 6;
-  const bool row_ok = qsel == 0 || has1;
-  const uint32_t* mymask = sMask + qsel * nwords;
-  const float sl2 = p.scale_log2;
-  const float last_bias = log2f((float)(p.Tk - (p.nkb - 1) * kBlock));
-  const int last_word = (p.nkb - 1) >> 5;
-  constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
-  constexpr uint32_t idO = idesc_bf16(kRows, D, true);
 
-  int k_issued = 0, v_issued = 0;  // thread 0 only
-  if (tid == 0 && ntiles > 0) {
-    load_kv_tile<D>(sK, &tmK, &tmKC, bar0 + 8 * K_FULL, sTiles[0], p.nkb, h, b);
-    load_kv_tile<D>(sV, &tmV, &tmVC, bar0 + 8 * V_FULL, sTiles[0], p.nkb, h, b);
-    k_issued = v_issued = 1;
-  }
-  float m_run = -INFINITY, l_run = 0.f;
-  int done = 0;
-  for (int i = 0; i < ntiles; ++i) {
-    const int entry = sTiles[i];
-    // -- thread 0: S = Q K^T --
-    if (tid == 0 && !*abort_flag) {
-      bool ok = true;
-      if (i == 0) ok = mbar_wait(bar0 + 8 * Q_FULL, 0, abort_flag, p.status);
-      if (ok && i > 0) {
-        // P V of the previous tile is complete: S/P columns and the V buffer are free.
-        ok = mbar_wait(bar0 + 8 * O_DONE, (i - 1) & 1, abort_flag, p.status);
-        if (ok) {
-          load_kv_tile<D>(sV, &tmV, &tmVC, bar0 + 8 * V_FULL, entry, p.nkb, h, b);
-          ++v_issued;
+  if (warp == kSoftmaxWarps) {
+    // ------------------------------------------------------------------ TMA + MMA thread
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
+      constexpr uint32_t idO = idesc_bf16(kRows, D, true);
+      const uint32_t tO = tmem + 128;
+      // Loads issued per ring slot (for the drain after an abort).
+      int k_loads0 = 0, k_loads1 = 0, v_loads0 = 0, v_loads1 = 0;
+      for (int t = 0; t < 2 && t < ntiles; ++t) {
+        load_kv_tile<D>(sK + t * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + t), sTiles[t], h, b);
+        load_kv_tile<D>(sV + t * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + t), sTiles[t], h, b);
+        if (t) ++k_loads1, ++v_loads1; else ++k_loads0, ++v_loads0;
+      }
+      bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag, p.status);
+      for (int i = 0; ok && i <= ntiles; ++i) {
+        if (i < ntiles) {
+          // S_i = Q K_i^T into S buffer i % 2
+          const int sl = i & 1;
+          const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+          ok = mbar_wait(bar(K_FULL0 + sl), ph, abort_flag, p.status);
+          if (ok && i >= 2) {
+            // P_{i-2} V_{i-2} is done: S buffer sl and V slot sl are free.
+            ok = mbar_wait(bar(PV_DONE0 + sl), ph ^ 1u, abort_flag, p.status);
+            if (ok) {
+              load_kv_tile<D>(sV + sl * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + sl), sTiles[i], h, b);
+              if (sl) ++v_loads1; else ++v_loads0;
+            }
+          }
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t kbase = sK + sl * L::kKVTile;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k)
+            mma_ss(tmem + (uint32_t)(kKeys * sl),
+                   smem_desc_sw128(sQ + (uint32_t)((k >> 2) * kQBox + (k & 3) * 32), 16, 1024),
+                   smem_desc_sw128(kbase + (uint32_t)((k >> 2) * kKVBox + (k & 3) * 32), 16, 1024),
+                   idS, k > 0 ? 1u : 0u);
+          mma_commit(bar(S_FULL0 + sl));
+        }
+        if (i >= 1) {
+          // O += P_{i-1} V_{i-1}
+          const int ps = (i - 1) & 1;
+          const uint32_t pph = (uint32_t)((i - 1) >> 1) & 1u;
+          ok = mbar_wait(bar(P_FULL0 + ps), pph, abort_flag, p.status) &&
+               mbar_wait(bar(V_FULL0 + ps), pph, abort_flag, p.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t vbase = sV + ps * L::kKVTile;
+#pragma unroll
+          for (int k = 0; k < kKeys / 16; ++k)
+            mma_ts(tO, tmem + (uint32_t)(kKeys * ps + 8 * k),
+                   smem_desc_sw128(vbase + (uint32_t)(k * 16 * 128), kKVBox, 1024), idO,
+                   (i > 1 || k > 0) ? 1u : 0u);
+          mma_commit(bar(PV_DONE0 + ps));
+        }
+        if (i + 2 < ntiles) {
+          // K slot i % 2 is free once S_i has completed.
+          const int sl = i & 1;
+          ok = mbar_wait(bar(S_FULL0 + sl), (uint32_t)(i >> 1) & 1u, abort_flag, p.status);
+          if (!ok) break;
+          load_kv_tile<D>(sK + sl * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + sl), sTiles[i + 2], h, b);
+          if (sl) ++k_loads1; else ++k_loads0;
         }
       }
-      if (ok) ok = mbar_wait(bar0 + 8 * K_FULL, i & 1, abort_flag, p.status);
-      if (ok) {
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (uint32_t)((k >> 2) * kBoxBytes + (k & 3) * 32);
-          mma_ss(tS, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(sK + off, 16, 1024), idS,
-                 k > 0 ? 1u : 0u);
-        }
-        mma_commit(bar0 + 8 * S_FULL);
+      // Every MMA of this CTA has completed once DRAIN fires.
+      mma_commit(bar(DRAIN));
+      mbar_wait_quiet(bar(DRAIN), 0);
+      if (*abort_flag) {  // never leave while a bulk copy may still write shared memory
+        mbar_wait_quiet(bar(Q_FULL), 0);
+        if (k_loads0) mbar_wait_quiet(bar(K_FULL0), (uint32_t)(k_loads0 - 1) & 1u);
+        if (k_loads1) mbar_wait_quiet(bar(K_FULL1), (uint32_t)(k_loads1 - 1) & 1u);
+        if (v_loads0) mbar_wait_quiet(bar(V_FULL0), (uint32_t)(v_loads0 - 1) & 1u);
+        if (v_loads1) mbar_wait_quiet(bar(V_FULL1), (uint32_t)(v_loads1 - 1) & 1u);
       }
     }
-    // -- all: softmax of this tile --
-    if (warp_wait(bar0 + 8 * S_FULL, i & 1, abort_flag, p.status)) {
-      tc_fence_after();
-      if (tid == 0 && i + 1 < ntiles) {  // the S MMA has released the K buffer
-        load_kv_tile<D>(sK, &tmK, &tmKC, bar0 + 8 * K_FULL, sTiles[i + 1], p.nkb, h, b);
-        ++k_issued;
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax warps
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;  // warp w reads TMEM lanes 32w..
+    const uint32_t tOr = tmem + 128 + lane_base;
+    const int row = warp * 32 + lane;
+    const int qsel = row >> 6;
+    const bool row_ok = qsel == 0 || has1;
+    const uint32_t* mymask = sMask + qsel * nwords;
+    const float sl2 = p.scale_log2;
+    const float last_bias = log2f((float)(p.Tk - (p.nkb - 1) * kBlock));
+    const int last_col = (p.nkb - 1) & 63;  // column of the last centroid in its 64-group
+    const int last_group = (p.nkb - 1) >> 6;
+    float m_run = -INFINITY, l_run = 0.f;
+    int i = 0;
+    bool ok = true;
+    for (; i < ntiles; ++i) {
+      const int sl = i & 1;
+      if (!warp_wait(bar(S_FULL0 + sl), (uint32_t)(i >> 1) & 1u, abort_flag, p.status)) {
+        ok = false;
+        break;
       }
-      uint32_t s[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tSr + 32 * c, s[c]);
+      tc_fence_after();
+      const uint32_t tSr = tmem + (uint32_t)(kKeys * sl) + lane_base;
+      uint32_t s[2][32];
+      tmem_ld32(tSr, s[0]);
+      tmem_ld32(tSr + 32, s[1]);
       tmem_wait_ld();
-      float mt = -INFINITY;
-      if (entry < 0) {
+      const int entry = sTiles[i];
+      const bool centroid = entry < 0;
+      // Row max in eight independent partials.  Exact tiles keep raw scores (max(s) * scale_log2
+      // equals max(s * scale_log2) bit for bit, the scale being positive) and fold the scale into
+      // the exponent's FMA; centroid columns get log2(len) added.
+      float mx[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx[j] = -INFINITY;
+      if (centroid) {
         const int t = -entry - 1;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int wi = 4 * t + c;
+        for (int c = 0; c < 2; ++c) {
+          const int wi = 2 * t + c;
           const uint32_t word = mymask[wi < nwords ? wi : nwords - 1];  // index kept in range
           const uint32_t approx = row_ok ? (~word & valid_word(wi, p.nkb)) : 0u;
-          const int last_j = wi == last_word ? ((p.nkb - 1) & 31) : 32;
+          const int lj = (t == last_group && (last_col >> 5) == c) ? (last_col & 31) : 32;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float bias = j == last_j ? last_bias : 6.f;  // log2(valid length)
+            const float bias = j == lj ? last_bias : 6.f;  // log2(valid length)
             const float v =
                 ((approx >> j) & 1u) ? fmaf(__uint_as_float(s[c][j]), sl2, bias) : -INFINITY;
             s[c][j] = __float_as_uint(v);
-            mt = fmaxf(mt, v);
+            mx[j & 7] = fmaxf(mx[j & 7], v);
           }
         }
       } else {
-        const int a = entry & 0xffff;
-        const int hi = (entry >> 16) & 0xffff;
-        const bool single = hi == kNoBlock;
-        const int bb = single ? a : hi;
-        const uint32_t wa = mymask[a >> 5], wb = mymask[bb >> 5];
-        const bool va = row_ok && ((wa >> (a & 31)) & 1u);
-        const bool vb = row_ok && !single && ((wb >> (bb & 31)) & 1u);
-        const int la = va ? min(kBlock, p.Tk - a * kBlock) : 0;
-        const int lb = vb ? min(kBlock, p.Tk - bb * kBlock) : 0;
+        const int kb = entry;
+        const bool va = row_ok && ((mymask[kb >> 5] >> (kb & 31)) & 1u);
+        const int len = va ? min(kBlock, p.Tk - kb * kBlock) : 0;
+        if (len == kBlock) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int lim = c < 2 ? la : lb;
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float v = ((c & 1) * 32 + j) < lim ? __uint_as_float(s[c][j]) * sl2 : -INFINITY;
-            s[c][j] = __float_as_uint(v);
-            mt = fmaxf(mt, v);
-          }
+            for (int j = 0; j < 32; ++j) mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(s[c][j]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float v = (32 * c + j) < len ? __uint_as_float(s[c][j]) : -INFINITY;
+              s[c][j] = __float_as_uint(v);
+              mx[j & 7] = fmaxf(mx[j & 7], v);
+            }
         }
       }
+      float m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      if (!centroid) m_tile *= sl2;  // -inf stays -inf
       // Lazy rescaling: the running max only moves when a row's max grows by more than 8
       // (a factor 256), so P stays <= 256 and O is rarely touched; O and l share the max.
-      const float m_new = fmaxf(m_run, mt);
+      const float m_new = fmaxf(m_run, m_tile);
       bool need = false;
       float alpha = 1.f;
       if (m_run == -INFINITY) {
@@ -385,7 +415,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         m_run = m_new;
       }
       if (__any_sync(0xffffffffu, need)) {
-        // P V of the previous tile completed before this tile's S was issued.
+        // O may only be touched once every P V issued so far (up to tile i-1) has completed.
+        if (!warp_wait(bar(PV_DONE0 + ((i - 1) & 1)), (uint32_t)((i - 1) >> 1) & 1u, abort_flag,
+                       p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
@@ -398,76 +434,56 @@ __global__ void __launch_bounds__(kThreads, 2)
         l_run *= alpha;
       }
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      float sum = 0.f;
-      uint32_t pk[2][32];
+      const float k_mul = centroid ? 1.f : sl2;  // exponent = s * k_mul - m_use
+      float sums[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int j = 0; j < 8; ++j) sums[j] = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const float p0 = fast_exp2(__uint_as_float(s[c][j]) - m_use);
-          const float p1 = fast_exp2(__uint_as_float(s[c][j + 1]) - m_use);
-          sum += p0 + p1;
-          pk[c >> 1][(c & 1) * 16 + j / 2] = pack_bf16(p0, p1);
+          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c][j]), k_mul, -m_use));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c][j + 1]), k_mul, -m_use));
+          sums[(j >> 1) & 7] += p0 + p1;
+          pk[c * 16 + j / 2] = pack_bf16(p0, p1);
         }
       }
-      l_run += sum;
-      tmem_st32(tSr, pk[0]);  // P (BF16 pairs) overwrites S columns 0..63
-      tmem_st32(tSr + 32, pk[1]);
+      l_run += ((sums[0] + sums[1]) + (sums[2] + sums[3])) +
+               ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+      tmem_st32(tSr, pk);  // P (BF16 pairs) over the first 32 columns of this S buffer
       tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(P_FULL0 + sl));
     }
-    tc_fence_before();
-    __syncthreads();
-    if (*abort_flag) break;  // read by every thread after the same barrier: uniform
-    // -- thread 0: O += P V --
-    if (tid == 0) {
+    // ---- epilogue: O / l -> BF16 ----
+    if (ok && ntiles > 0 &&
+        warp_wait(bar(PV_DONE0 + ((ntiles - 1) & 1)), (uint32_t)((ntiles - 1) >> 1) & 1u,
+                  abort_flag, p.status)) {
       tc_fence_after();
-      if (mbar_wait(bar0 + 8 * V_FULL, i & 1, abort_flag, p.status)) {
-#pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k)
-          mma_ts(tO, tS + (uint32_t)(k * 8),
-                 smem_desc_sw128(sV + (uint32_t)(k * 16 * 128), kBoxBytes, 1024), idO,
-                 (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit(bar0 + 8 * O_DONE);
-      }
-    }
-    done = i + 1;
-  }
-
-  // ---- epilogue ----
-  if (ntiles > 0 && done == ntiles &&
-      warp_wait(bar0 + 8 * O_DONE, (ntiles - 1) & 1, abort_flag, p.status)) {
-    tc_fence_after();
-    const float inv = 1.f / l_run;
-    const int grow = qb0 * kBlock + row;
-    __nv_bfloat16* dst = p.out + (((int64_t)b * p.Tq + grow) * p.H + h) * D;
+      const float inv = 1.f / l_run;
+      const int grow = qb0 * kBlock + row;
+      __nv_bfloat16* dst = p.out + (((int64_t)b * p.Tq + grow) * p.H + h) * D;
 #pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t o[32];
-      tmem_ld32(tOr + 32 * c, o);
-      tmem_wait_ld();
-      if (grow < p.Tq) {
-        uint4 v4[4];
-        uint32_t* w32 = reinterpret_cast<uint32_t*>(v4);
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tOr + 32 * c, o);
+        tmem_wait_ld();
+        if (grow < p.Tq) {
+          uint4 v4[4];
+          uint32_t* w32 = reinterpret_cast<uint32_t*>(v4);
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          w32[j] = pack_bf16(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
-        uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+          for (int j = 0; j < 16; ++j)
+            w32[j] = pack_bf16(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) d4[j] = v4[j];
+          for (int j = 0; j < 4; ++j) d4[j] = v4[j];
+        }
       }
     }
   }
 
-  // ---- drain and release ----
-  if (tid == 0) {
-    mma_commit(bar0 + 8 * DRAIN);  // every MMA of this CTA has completed once this fires
-    mbar_wait_quiet(bar0 + 8 * DRAIN, 0);
-    if (*abort_flag) {  // never leave while a bulk copy may still write shared memory
-      mbar_wait_quiet(bar0 + 8 * Q_FULL, 0);
-      if (k_issued > 0) mbar_wait_quiet(bar0 + 8 * K_FULL, (k_issued - 1) & 1);
-      if (v_issued > 0) mbar_wait_quiet(bar0 + 8 * V_FULL, (v_issued - 1) & 1);
-    }
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -545,7 +561,11 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
 
 }  // namespace
 
-bool attn_sm100_supported(const AttnParams& p) { return p.nkb <= kMaxKeyBlocks; }
+// The softmax folds a positive scale into the exponent (max(s) * scale == max(s * scale) and
+// masked -inf scores stay -inf), so other scales take the mma.sync kernel.
+bool attn_sm100_supported(const AttnParams& p) {
+  return p.nkb <= kMaxKeyBlocks && p.scale_log2 > 0.f;
+}
 
 cudaError_t launch_attn_sm100(const AttnParams& p, int D, cudaStream_t stream) {
   return D == 128 ? launch_sm100<128>(p, stream) : launch_sm100<64>(p, stream);

@@ -155,9 +155,14 @@ __device__ __forceinline__ void routing_dot2(const float* qa, const float* qb,
   float pa[8], pb[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) pa[j] = pb[j] = 0.f;
-#pragma unroll 4
-  for (int i = 0; i < D / 8; ++i) {
-    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(kcrow) + i);
+  uint4 rows[16];  // D <= 128: the whole centroid row in flight at once
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < D / 8) rows[i] = __ldg(reinterpret_cast<const uint4*>(kcrow) + i);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i >= D / 8) break;
+    const uint4 raw = rows[i];
     const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
