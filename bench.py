@@ -52,13 +52,14 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def ncu_traffic():
-    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary, if any."""
-    f = ROOT / "profiles" / "ncu_traffic.txt"
+def ncu_traffic(heads):
+    """DRAM bytes (read + write) of one attention launch over `heads` heads, from the committed
+    ncu summary of the full 24-head launch (traffic scales with the head count), if present."""
+    f = ROOT / "profiles" / "attn_sm100_video_dit_t32k_h8.md"
     try:
         for line in f.read_text().splitlines():
             if line.startswith("attention_bytes_per_launch="):
-                return float(line.split("=", 1)[1])
+                return float(line.split("=", 1)[1]) * heads / H
     except OSError:
         pass
     return None
@@ -343,15 +344,16 @@ def main():
             "kernel_ms": {"pool": pool_ms, "threshold": thr_ms, "attention": attn_ms},
             "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": attn_tflops / pk["bf16_tflops"],
-                         "traffic": ncu_traffic(), "kernel": "attention (fused routed)",
+                         "traffic": ncu_traffic(h1 - h0), "kernel": "attention (fused routed)",
                          "algorithmic_flops_per_launch": attn_flops, "peak_source": pk_kind},
             "pool_roofline": {"bound": "hbm", "achieved": pool_gbs, "peak": pk["hbm_gbs"],
                               "unit": "GB/s", "frac": pool_gbs / pk["hbm_gbs"],
                               "bytes_per_launch": pool_bytes, "peak_source": pk_kind},
             "cpu_baseline": cpu,
-            "e2e": {"value": dense_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
-                    "ms_per_call": e2e_ms, "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world},
+            "e2e": None if args.no_e2e else {
+                "value": dense_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+                "ms_per_call": e2e_ms, "h2d_bytes_per_step": h2d * world,
+                "d2h_bytes_per_step": d2h * world},
             "gpu_launches": st.launches() * args.steps * world,
             "clocks": clk.summary(),
         }
