@@ -1,7 +1,7 @@
 // Fused routed attention on the Blackwell data path (replaces `_sol`, kernels.py:101-182).
 //
 // One CTA = one 128-row query tile = two 64-row q-blocks (qb0 = 2*x, qb0 + 1) of one (b, h);
-// 160 threads, two CTAs per SM (256 TMEM columns and ~100 KB of shared memory each).
+// 192 threads, two CTAs per SM (256 TMEM columns and ~100 KB of shared memory each).
 //
 // Tiles hold 64 keys: one exact key block, or 64 pooled centroids.  The tile list (shared
 // memory, built by warp 0 after routing) holds first every 64-centroid group that still has a
@@ -10,12 +10,17 @@
 // an exact block sees it as -inf; a centroid whose block is exact for the row's q-block too.
 //
 // Warp roles:
-//   warps 0-3  softmax: warp w owns TMEM lanes / tile rows 32w..32w+31.  Per tile: wait S_FULL,
-//              tcgen05.ld S, mask/bias, FP32 online softmax with lazy rescaling, P (BF16) written
-//              over its S buffer, arrive P_FULL.  Epilogue O / l -> BF16.
-//   warp 4     TMA + MMA issue (lane 0): Q once; K and V through 2-slot rings; for tile i it
-//              issues S_i = Q K_i^T into TMEM buffer i%2, then O += P_{i-1} V_{i-1}, so the
-//              tensor core works on S_{i+1} and P V while the softmax warps work on tile i.
+//   warps 0-3  softmax: warp w owns TMEM lanes / tile rows 32w..32w+31 (warps 0-1 q-block qb0,
+//              warps 2-3 qb0 + 1).  Per tile: wait S_FULL, tcgen05.ld S, mask/bias, FP32 online
+//              softmax with lazy rescaling, P (BF16) written over its S buffer, arrive P_FULL.
+//              A warp whose q-block does not use the tile writes P = 0 without reading S.
+//              Epilogue O / l -> BF16.
+//   warp 4     MMA issue (the whole warp runs the loop, lane 0 issues): S_i = Q K_i^T into
+//              TMEM buffer i % 2, then O += P_{i-1} V_{i-1}, so the tensor core works on S_{i+1}
+//              and P V while the softmax warps work on tile i.
+//   warp 5     TMA producer (lane 0): Q once, then K and V through 2-slot rings, refilling a K
+//              slot when its S MMAs have completed (K_EMPTY) and a V slot when its P V MMAs have
+//              completed (PV_DONE).
 // TMEM: S buffers at columns [0, 64) and [64, 128) (P packed into the first 32 columns of its
 // buffer), O at [128, 128 + D).
 #include <cudaTypedefs.h>
@@ -31,7 +36,9 @@ using namespace sm100;
 constexpr int kRows = 128;         // query rows per CTA
 constexpr int kKeys = 64;          // keys per tile
 constexpr int kSoftmaxWarps = 4;
-constexpr int kThreads = 32 * (kSoftmaxWarps + 1);
+constexpr int kMmaWarp = 4;
+constexpr int kTmaWarp = 5;
+constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 256;
 constexpr int kQBox = kRows * 128;   // one 128-row x 64-column BF16 box of Q (16 KB)
 constexpr int kKVBox = kKeys * 128;  // one 64-row x 64-column BF16 box of K or V (8 KB)
@@ -40,7 +47,7 @@ constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
 // Barriers: slot-indexed pairs for the 2-deep rings.
 enum Bar {
   Q_FULL,
-  K_FULL0, K_FULL1, V_FULL0, V_FULL1,
+  K_FULL0, K_FULL1, K_EMPTY0, K_EMPTY1, V_FULL0, V_FULL1,
   S_FULL0, S_FULL1, P_FULL0, P_FULL1, PV_DONE0, PV_DONE1,
   DRAIN, NBARS
 };
@@ -103,6 +110,21 @@ __device__ __forceinline__ void load_kv_tile(uint32_t dst, const CUtensorMap* ti
     tma_load_4d(dst + j * kKVBox, cent ? cent_map : tile_map, full, 64 * j, row, h, b);
 }
 
+// Row max of 64 scores with three-input max instructions: eight independent chains.
+__device__ __forceinline__ float row_max64(const uint32_t (&s)[2][32]) {
+  float m[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const int c = g >> 2, j = (g & 3) * 8;
+    const float a = fmax3(__uint_as_float(s[c][j]), __uint_as_float(s[c][j + 1]),
+                          __uint_as_float(s[c][j + 2]));
+    const float b2 = fmax3(__uint_as_float(s[c][j + 3]), __uint_as_float(s[c][j + 4]),
+                           __uint_as_float(s[c][j + 5]));
+    m[g] = fmax3(a, b2, fmaxf(__uint_as_float(s[c][j + 6]), __uint_as_float(s[c][j + 7])));
+  }
+  return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
 }  // namespace
 
 
@@ -159,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (tid == kSoftmaxWarps * 32) {  // the TMA/MMA thread starts Q early
+  if (tid == kTmaWarp * 32) {  // the producer starts Q early
     tma_prefetch(&tmQ);
     tma_prefetch(&tmK);
     tma_prefetch(&tmV);
@@ -250,74 +272,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   const int ntiles = (int)misc[2];
 
-
-  if (warp == kSoftmaxWarps) {
-    // ------------------------------------------------------------------ TMA + MMA thread
+  if (warp == kTmaWarp) {
+    // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
-      constexpr uint32_t idO = idesc_bf16(kRows, D, true);
-      const uint32_t tO = tmem + 128;
       // Loads issued per ring slot (for the drain after an abort).
       int k_loads0 = 0, k_loads1 = 0, v_loads0 = 0, v_loads1 = 0;
-      for (int t = 0; t < 2 && t < ntiles; ++t) {
-        load_kv_tile<D>(sK + t * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + t), sTiles[t], h, b);
-        load_kv_tile<D>(sV + t * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + t), sTiles[t], h, b);
-        if (t) ++k_loads1, ++v_loads1; else ++k_loads0, ++v_loads0;
+      for (int i = 0; i < ntiles; ++i) {
+        const int sl = i & 1;
+        const uint32_t prev = (uint32_t)((i >> 1) - 1) & 1u;  // parity of this slot's last use
+        // K slot sl is free once S_{i-2} has completed; V slot sl once P_{i-2} V_{i-2} has.
+        if (i >= 2 && !mbar_wait(bar(K_EMPTY0 + sl), prev, abort_flag, p.status)) break;
+        load_kv_tile<D>(sK + sl * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + sl), sTiles[i], h, b);
+        if (sl) ++k_loads1; else ++k_loads0;
+        if (i >= 2 && !mbar_wait(bar(PV_DONE0 + sl), prev, abort_flag, p.status)) break;
+        load_kv_tile<D>(sV + sl * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + sl), sTiles[i], h, b);
+        if (sl) ++v_loads1; else ++v_loads0;
       }
-      bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag, p.status);
-      for (int i = 0; ok && i <= ntiles; ++i) {
-        if (i < ntiles) {
-          // S_i = Q K_i^T into S buffer i % 2
-          const int sl = i & 1;
-          const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-          ok = mbar_wait(bar(K_FULL0 + sl), ph, abort_flag, p.status);
-          if (ok && i >= 2) {
-            // P_{i-2} V_{i-2} is done: S buffer sl and V slot sl are free.
-            ok = mbar_wait(bar(PV_DONE0 + sl), ph ^ 1u, abort_flag, p.status);
-            if (ok) {
-              load_kv_tile<D>(sV + sl * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + sl), sTiles[i], h, b);
-              if (sl) ++v_loads1; else ++v_loads0;
-            }
-          }
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t kbase = sK + sl * L::kKVTile;
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k)
-            mma_ss(tmem + (uint32_t)(kKeys * sl),
-                   smem_desc_sw128(sQ + (uint32_t)((k >> 2) * kQBox + (k & 3) * 32), 16, 1024),
-                   smem_desc_sw128(kbase + (uint32_t)((k >> 2) * kKVBox + (k & 3) * 32), 16, 1024),
-                   idS, k > 0 ? 1u : 0u);
-          mma_commit(bar(S_FULL0 + sl));
-        }
-        if (i >= 1) {
-          // O += P_{i-1} V_{i-1}
-          const int ps = (i - 1) & 1;
-          const uint32_t pph = (uint32_t)((i - 1) >> 1) & 1u;
-          ok = mbar_wait(bar(P_FULL0 + ps), pph, abort_flag, p.status) &&
-               mbar_wait(bar(V_FULL0 + ps), pph, abort_flag, p.status);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t vbase = sV + ps * L::kKVTile;
-#pragma unroll
-          for (int k = 0; k < kKeys / 16; ++k)
-            mma_ts(tO, tmem + (uint32_t)(kKeys * ps + 8 * k),
-                   smem_desc_sw128(vbase + (uint32_t)(k * 16 * 128), kKVBox, 1024), idO,
-                   (i > 1 || k > 0) ? 1u : 0u);
-          mma_commit(bar(PV_DONE0 + ps));
-        }
-        if (i + 2 < ntiles) {
-          // K slot i % 2 is free once S_i has completed.
-          const int sl = i & 1;
-          ok = mbar_wait(bar(S_FULL0 + sl), (uint32_t)(i >> 1) & 1u, abort_flag, p.status);
-          if (!ok) break;
-          load_kv_tile<D>(sK + sl * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + sl), sTiles[i + 2], h, b);
-          if (sl) ++k_loads1; else ++k_loads0;
-        }
-      }
-      // Every MMA of this CTA has completed once DRAIN fires.
-      mma_commit(bar(DRAIN));
-      mbar_wait_quiet(bar(DRAIN), 0);
       if (*abort_flag) {  // never leave while a bulk copy may still write shared memory
         mbar_wait_quiet(bar(Q_FULL), 0);
         if (k_loads0) mbar_wait_quiet(bar(K_FULL0), (uint32_t)(k_loads0 - 1) & 1u);
@@ -327,81 +297,173 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issue
+    // The whole warp runs the loop so that descriptors and addresses stay warp-uniform; lane 0
+    // issues every MMA and commit (a commit tracks the MMAs of its own thread).
+    constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
+    constexpr uint32_t idO = idesc_bf16(kRows, D, true);
+    constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
+    const uint64_t dQ = smem_desc_sw128(sQ, 16, 1024);
+    const uint64_t dK = smem_desc_sw128(sK, 16, 1024);
+    const uint64_t dV = smem_desc_sw128(sV, kKVBox, 1024);
+    const uint32_t tO = tmem + 128;
+    bool ok = warp_wait(bar(Q_FULL), 0, abort_flag, p.status);
+    for (int i = 0; ok && i <= ntiles; ++i) {
+      if (i < ntiles) {
+        // S_i = Q K_i^T into S buffer i % 2, once K_i has landed and P_{i-2} V_{i-2} (the last
+        // reader of that buffer) has completed.
+        const int sl = i & 1;
+        const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+        ok = warp_wait(bar(K_FULL0 + sl), ph, abort_flag, p.status) &&
+             (i < 2 || warp_wait(bar(PV_DONE0 + sl), ph ^ 1u, abort_flag, p.status));
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t kd = dK + (uint64_t)sl * kSlotStep;
+          const uint32_t tS = tmem + (uint32_t)(kKeys * sl);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t off = (uint64_t)(((k >> 2) * kQBox + (k & 3) * 32) >> 4);
+            const uint64_t offk = (uint64_t)(((k >> 2) * kKVBox + (k & 3) * 32) >> 4);
+            mma_ss(tS, dQ + off, kd + offk, idS, k > 0 ? 1u : 0u);
+          }
+          mma_commit(bar(S_FULL0 + sl));
+          mma_commit(bar(K_EMPTY0 + sl));
+        }
+        __syncwarp();
+      }
+      if (i >= 1) {
+        // O += P_{i-1} V_{i-1}
+        const int ps = (i - 1) & 1;
+        const uint32_t pph = (uint32_t)((i - 1) >> 1) & 1u;
+        ok = warp_wait(bar(P_FULL0 + ps), pph, abort_flag, p.status) &&
+             warp_wait(bar(V_FULL0 + ps), pph, abort_flag, p.status);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t vd = dV + (uint64_t)ps * kSlotStep;
+          const uint32_t tP = tmem + (uint32_t)(kKeys * ps);
+#pragma unroll
+          for (int k = 0; k < kKeys / 16; ++k)
+            mma_ts(tO, tP + (uint32_t)(8 * k), vd + (uint64_t)((k * 16 * 128) >> 4), idO,
+                   (i > 1 || k > 0) ? 1u : 0u);
+          mma_commit(bar(PV_DONE0 + ps));
+        }
+        __syncwarp();
+      }
+    }
+    // Every MMA of this CTA has completed once DRAIN fires.
+    if (lane == 0) {
+      mma_commit(bar(DRAIN));
+      mbar_wait_quiet(bar(DRAIN), 0);
+    }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax warps
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;  // warp w reads TMEM lanes 32w..
     const uint32_t tOr = tmem + 128 + lane_base;
     const int row = warp * 32 + lane;
-    const int qsel = row >> 6;
-    const bool row_ok = qsel == 0 || has1;
+    const int qsel = warp >> 1;                    // warps 0-1: qb0, warps 2-3: qb0 + 1
+    const bool warp_rows = qsel == 0 || has1;      // the warp's q-block exists
     const uint32_t* mymask = sMask + qsel * nwords;
     const float sl2 = p.scale_log2;
-    const float last_bias = log2f((float)(p.Tk - (p.nkb - 1) * kBlock));
-    const int last_col = (p.nkb - 1) & 63;  // column of the last centroid in its 64-group
+    const uint64_t sl2x2 = f2_pack(sl2, sl2);
+    const uint64_t six2 = f2_pack(6.f, 6.f);       // log2(64): bias of a full block's centroid
+    const int last_len = p.Tk - (p.nkb - 1) * kBlock;
+    const float last_bias = log2f((float)last_len);
+    const int last_col = (p.nkb - 1) & 63;         // column of the last centroid in its group
     const int last_group = (p.nkb - 1) >> 6;
     float m_run = -INFINITY, l_run = 0.f;
     int i = 0;
     bool ok = true;
     for (; i < ntiles; ++i) {
       const int sl = i & 1;
+      // Tile metadata first: these shared-memory reads overlap the wait for S.  Every value
+      // below is warp-uniform (one q-block per warp).
+      const int entry = sTiles[i];
+      const bool centroid = entry < 0;
+      uint32_t approx0 = 0u, approx1 = 0u;  // centroid columns this q-block uses
+      int len = 0;                          // valid keys of an exact block it selected
+      if (centroid) {
+        const int t = -entry - 1;  // 2t < nwords since t <= (nkb - 1) / 64
+        if (warp_rows) {
+          approx0 = ~mymask[2 * t] & valid_word(2 * t, p.nkb);
+          if (2 * t + 1 < nwords) approx1 = ~mymask[2 * t + 1] & valid_word(2 * t + 1, p.nkb);
+        }
+      } else if (warp_rows && ((mymask[entry >> 5] >> (entry & 31)) & 1u)) {
+        len = min(kBlock, p.Tk - entry * kBlock);
+      }
+      const bool active = centroid ? (approx0 | approx1) != 0u : len > 0;
       if (!warp_wait(bar(S_FULL0 + sl), (uint32_t)(i >> 1) & 1u, abort_flag, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t tSr = tmem + (uint32_t)(kKeys * sl) + lane_base;
+      if (!active) {
+        // The tile contributes nothing to these rows: P = 0, the running max and sum stay.
+        uint32_t z[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) z[j] = 0u;
+        tmem_st32(tSr, z);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(P_FULL0 + sl));
+        continue;
+      }
       uint32_t s[2][32];
       tmem_ld32(tSr, s[0]);
       tmem_ld32(tSr + 32, s[1]);
       tmem_wait_ld();
-      const int entry = sTiles[i];
-      const bool centroid = entry < 0;
-      // Row max in eight independent partials.  Exact tiles keep raw scores (max(s) * scale_log2
-      // equals max(s * scale_log2) bit for bit, the scale being positive) and fold the scale into
-      // the exponent's FMA; centroid columns get log2(len) added.
-      float mx[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) mx[j] = -INFINITY;
+      float m_tile, k_mul;
       if (centroid) {
+        // Centroid logits in log2 units, s * scale_log2 + log2(len), and -inf where the block is
+        // exact for this q-block (or past the last block).
         const int t = -entry - 1;
+        if (t == last_group && last_len != kBlock) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int wi = 2 * t + c;
-          const uint32_t word = mymask[wi < nwords ? wi : nwords - 1];  // index kept in range
-          const uint32_t approx = row_ok ? (~word & valid_word(wi, p.nkb)) : 0u;
-          const int lj = (t == last_group && (last_col >> 5) == c) ? (last_col & 31) : 32;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float bias = j == lj ? last_bias : 6.f;  // log2(valid length)
-            const float v =
-                ((approx >> j) & 1u) ? fmaf(__uint_as_float(s[c][j]), sl2, bias) : -INFINITY;
-            s[c][j] = __float_as_uint(v);
-            mx[j & 7] = fmaxf(mx[j & 7], v);
-          }
-        }
-      } else {
-        const int kb = entry;
-        const bool va = row_ok && ((mymask[kb >> 5] >> (kb & 31)) & 1u);
-        const int len = va ? min(kBlock, p.Tk - kb * kBlock) : 0;
-        if (len == kBlock) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(s[c][j]));
-        } else {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t approx = c ? approx1 : approx0;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float v = (32 * c + j) < len ? __uint_as_float(s[c][j]) : -INFINITY;
+              const float bias = (32 * c + j) == last_col ? last_bias : 6.f;
+              const float v = ((approx >> j) & 1u) ? fmaf(__uint_as_float(s[c][j]), sl2, bias)
+                                                   : -INFINITY;
               s[c][j] = __float_as_uint(v);
-              mx[j & 7] = fmaxf(mx[j & 7], v);
             }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t approx = c ? approx1 : approx0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              float v0, v1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c][j]), __uint_as_float(s[c][j + 1])),
+                               sl2x2, six2),
+                        v0, v1);
+              s[c][j] = __float_as_uint(((approx >> j) & 1u) ? v0 : -INFINITY);
+              s[c][j + 1] = __float_as_uint(((approx >> (j + 1)) & 1u) ? v1 : -INFINITY);
+            }
+          }
         }
+        m_tile = row_max64(s);
+        k_mul = 1.f;
+      } else {
+        // Exact tiles keep raw scores: max(s) * scale_log2 equals max(s * scale_log2) bit for
+        // bit (the scale is positive) and the scale is folded into the exponent's FMA.
+        if (len < kBlock) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (32 * c + j >= len) s[c][j] = __float_as_uint(-INFINITY);
+        }
+        m_tile = row_max64(s) * sl2;
+        k_mul = sl2;
       }
-      float m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      if (!centroid) m_tile *= sl2;  // -inf stays -inf
       // Lazy rescaling: the running max only moves when a row's max grows by more than 8
       // (a factor 256), so P stays <= 256 and O is rarely touched; O and l share the max.
       const float m_new = fmaxf(m_run, m_tile);
@@ -412,46 +474,62 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else if (m_new > m_run + 8.f) {
         need = true;
         alpha = fast_exp2(m_run - m_new);
+        l_run *= alpha;  // before this tile's sum, which uses the new max
         m_run = m_new;
       }
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
+      // p = exp2(s * k_mul - m_use), two lanes per FMA; sums in four packed accumulators.
+      const uint64_t kmul2 = f2_pack(k_mul, k_mul), negm2 = f2_pack(-m_use, -m_use);
+      uint64_t acc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = 0ull;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c][j]), __uint_as_float(s[c][j + 1])), kmul2,
+                           negm2),
+                    x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          acc[(j >> 1) & 3] = f2_add(acc[(j >> 1) & 3], f2_pack(p0, p1));
+          pk[c * 16 + j / 2] = pack_bf16(p0, p1);
+        }
+      }
+      {
+        const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+        float lo, hi;
+        f2_unpack(f2_add(a01, a23), lo, hi);
+        l_run += lo + hi;
+      }
+      tmem_st32(tSr, pk);  // P (BF16 pairs) over the first 32 columns of this S buffer
       if (__any_sync(0xffffffffu, need)) {
-        // O may only be touched once every P V issued so far (up to tile i-1) has completed.
+        // O may only be touched once every P V issued so far (up to tile i-1) has completed;
+        // P_i V_i is not issued before this warp arrives on P_FULL below.
         if (!warp_wait(bar(PV_DONE0 + ((i - 1) & 1)), (uint32_t)((i - 1) >> 1) & 1u, abort_flag,
                        p.status)) {
+          tmem_wait_st();
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(tOr + 32 * c, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+          for (int j = 0; j < 32; j += 2) {
+            float x0, x1;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), a2), x0, x1);
+            o[j] = __float_as_uint(x0);
+            o[j + 1] = __float_as_uint(x1);
+          }
           tmem_st32(tOr + 32 * c, o);
         }
-        l_run *= alpha;
       }
-      const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      const float k_mul = centroid ? 1.f : sl2;  // exponent = s * k_mul - m_use
-      float sums[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sums[j] = 0.f;
-      uint32_t pk[32];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c][j]), k_mul, -m_use));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c][j + 1]), k_mul, -m_use));
-          sums[(j >> 1) & 7] += p0 + p1;
-          pk[c * 16 + j / 2] = pack_bf16(p0, p1);
-        }
-      }
-      l_run += ((sums[0] + sums[1]) + (sums[2] + sums[3])) +
-               ((sums[4] + sums[5]) + (sums[6] + sums[7]));
-      tmem_st32(tSr, pk);  // P (BF16 pairs) over the first 32 columns of this S buffer
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
