@@ -15,12 +15,14 @@
 //              softmax with lazy rescaling, P (BF16) written over its S buffer, arrive P_FULL.
 //              A warp whose q-block does not use the tile writes P = 0 without reading S.
 //              Epilogue O / l -> BF16.
-//   warp 4     MMA issue (the whole warp runs the loop, lane 0 issues): S_i = Q K_i^T into
-//              TMEM buffer i % 2, then O += P_{i-1} V_{i-1}, so the tensor core works on S_{i+1}
-//              and P V while the softmax warps work on tile i.
-//   warp 5     TMA producer (lane 0): Q once, then K and V through 2-slot rings, refilling a K
-//              slot when its S MMAs have completed (K_EMPTY) and a V slot when its P V MMAs have
-//              completed (PV_DONE).
+//   warp 4     S issue (the whole warp runs the loop, lane 0 issues): S_i = Q K_i^T into TMEM
+//              buffer i % 2 once P_{i-2} V_{i-2} has freed it; refills the K ring (2 slots)
+//              when S_{i-1} has completed (K_EMPTY).
+//   warp 5     P V issue: O += P_i V_i once the softmax warps have written P_i; loads Q and
+//              refills the V ring when P_i V_i has completed (PV_DONE).
+//   One thread can issue a tcgen05.mma only about every 100 cycles, so S (8 MMAs of N=64 per
+//   tile) and P V (4 MMAs of N=D) come from two threads; the tensor core works on S_{i+1} and
+//   P_{i-1} V_{i-1} while the softmax warps work on tile i.
 // TMEM: S buffers at columns [0, 64) and [64, 128) (P packed into the first 32 columns of its
 // buffer), O at [128, 128 + D).
 #include <cudaTypedefs.h>
@@ -36,8 +38,8 @@ using namespace sm100;
 constexpr int kRows = 128;         // query rows per CTA
 constexpr int kKeys = 64;          // keys per tile
 constexpr int kSoftmaxWarps = 4;
-constexpr int kMmaWarp = 4;
-constexpr int kTmaWarp = 5;
+constexpr int kSWarp = 4;   // S = Q K^T issue and the K ring
+constexpr int kPVWarp = 5;  // O += P V issue, the V ring and Q
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 256;
 constexpr int kQBox = kRows * 128;   // one 128-row x 64-column BF16 box of Q (16 KB)
@@ -49,7 +51,7 @@ enum Bar {
   Q_FULL,
   K_FULL0, K_FULL1, K_EMPTY0, K_EMPTY1, V_FULL0, V_FULL1,
   S_FULL0, S_FULL1, P_FULL0, P_FULL1, PV_DONE0, PV_DONE1,
-  DRAIN, NBARS
+  DRAIN_S, DRAIN_PV, NBARS
 };
 
 template <int D>
@@ -181,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (tid == kTmaWarp * 32) {  // the producer starts Q early
+  if (tid == kPVWarp * 32) {  // Q starts loading before the routing prologue
     tma_prefetch(&tmQ);
     tma_prefetch(&tmK);
     tma_prefetch(&tmV);
@@ -272,91 +274,118 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   const int ntiles = (int)misc[2];
 
-  if (warp == kTmaWarp) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      // Loads issued per ring slot (for the drain after an abort).
-      int k_loads0 = 0, k_loads1 = 0, v_loads0 = 0, v_loads1 = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        const int sl = i & 1;
-        const uint32_t prev = (uint32_t)((i >> 1) - 1) & 1u;  // parity of this slot's last use
-        // K slot sl is free once S_{i-2} has completed; V slot sl once P_{i-2} V_{i-2} has.
-        if (i >= 2 && !mbar_wait(bar(K_EMPTY0 + sl), prev, abort_flag, p.status)) break;
-        load_kv_tile<D>(sK + sl * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + sl), sTiles[i], h, b);
-        if (sl) ++k_loads1; else ++k_loads0;
-        if (i >= 2 && !mbar_wait(bar(PV_DONE0 + sl), prev, abort_flag, p.status)) break;
-        load_kv_tile<D>(sV + sl * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + sl), sTiles[i], h, b);
-        if (sl) ++v_loads1; else ++v_loads0;
-      }
-      if (*abort_flag) {  // never leave while a bulk copy may still write shared memory
-        mbar_wait_quiet(bar(Q_FULL), 0);
-        if (k_loads0) mbar_wait_quiet(bar(K_FULL0), (uint32_t)(k_loads0 - 1) & 1u);
-        if (k_loads1) mbar_wait_quiet(bar(K_FULL1), (uint32_t)(k_loads1 - 1) & 1u);
-        if (v_loads0) mbar_wait_quiet(bar(V_FULL0), (uint32_t)(v_loads0 - 1) & 1u);
-        if (v_loads1) mbar_wait_quiet(bar(V_FULL1), (uint32_t)(v_loads1 - 1) & 1u);
-      }
-    }
-    __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issue
+  if (warp == kSWarp) {
+    // ------------------------------------------------------------------ S issue + K ring
     // The whole warp runs the loop so that descriptors and addresses stay warp-uniform; lane 0
-    // issues every MMA and commit (a commit tracks the MMAs of its own thread).
+    // issues every copy, MMA and commit (a commit tracks the MMAs of its own thread).  S and
+    // P V are issued by two different warps: one thread can issue a tcgen05.mma only every
+    // ~100 cycles, more than an M=128 N=64 MMA computes.
     constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
-    constexpr uint32_t idO = idesc_bf16(kRows, D, true);
     constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
     const uint64_t dQ = smem_desc_sw128(sQ, 16, 1024);
     const uint64_t dK = smem_desc_sw128(sK, 16, 1024);
-    const uint64_t dV = smem_desc_sw128(sV, kKVBox, 1024);
-    const uint32_t tO = tmem + 128;
-    bool ok = warp_wait(bar(Q_FULL), 0, abort_flag, p.status);
-    for (int i = 0; ok && i <= ntiles; ++i) {
-      if (i < ntiles) {
-        // S_i = Q K_i^T into S buffer i % 2, once K_i has landed and P_{i-2} V_{i-2} (the last
-        // reader of that buffer) has completed.
-        const int sl = i & 1;
-        const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-        ok = warp_wait(bar(K_FULL0 + sl), ph, abort_flag, p.status) &&
-             (i < 2 || warp_wait(bar(PV_DONE0 + sl), ph ^ 1u, abort_flag, p.status));
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint64_t kd = dK + (uint64_t)sl * kSlotStep;
-          const uint32_t tS = tmem + (uint32_t)(kKeys * sl);
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint64_t off = (uint64_t)(((k >> 2) * kQBox + (k & 3) * 32) >> 4);
-            const uint64_t offk = (uint64_t)(((k >> 2) * kKVBox + (k & 3) * 32) >> 4);
-            mma_ss(tS, dQ + off, kd + offk, idS, k > 0 ? 1u : 0u);
-          }
-          mma_commit(bar(S_FULL0 + sl));
-          mma_commit(bar(K_EMPTY0 + sl));
-        }
-        __syncwarp();
-      }
-      if (i >= 1) {
-        // O += P_{i-1} V_{i-1}
-        const int ps = (i - 1) & 1;
-        const uint32_t pph = (uint32_t)((i - 1) >> 1) & 1u;
-        ok = warp_wait(bar(P_FULL0 + ps), pph, abort_flag, p.status) &&
-             warp_wait(bar(V_FULL0 + ps), pph, abort_flag, p.status);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint64_t vd = dV + (uint64_t)ps * kSlotStep;
-          const uint32_t tP = tmem + (uint32_t)(kKeys * ps);
-#pragma unroll
-          for (int k = 0; k < kKeys / 16; ++k)
-            mma_ts(tO, tP + (uint32_t)(8 * k), vd + (uint64_t)((k * 16 * 128) >> 4), idO,
-                   (i > 1 || k > 0) ? 1u : 0u);
-          mma_commit(bar(PV_DONE0 + ps));
-        }
-        __syncwarp();
+    int k_loads0 = 0, k_loads1 = 0;  // copies issued per slot (for the drain after an abort)
+    if (lane == 0) {
+      for (int t = 0; t < 2 && t < ntiles; ++t) {
+        load_kv_tile<D>(sK + t * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + t), sTiles[t], h, b);
+        if (t) ++k_loads1; else ++k_loads0;
       }
     }
-    // Every MMA of this CTA has completed once DRAIN fires.
+    bool ok = warp_wait(bar(Q_FULL), 0, abort_flag, p.status);
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const int sl = i & 1;
+      const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+      if (i >= 1 && i + 1 < ntiles) {
+        // K slot (i + 1) % 2 is free once S_{i-1} has completed.
+        const int fs = (i - 1) & 1;
+        ok = warp_wait(bar(K_EMPTY0 + fs), (uint32_t)((i - 1) >> 1) & 1u, abort_flag, p.status);
+        if (!ok) break;
+        if (lane == 0) {
+          load_kv_tile<D>(sK + fs * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + fs), sTiles[i + 1], h, b);
+          if (fs) ++k_loads1; else ++k_loads0;
+        }
+      }
+      // S_i = Q K_i^T into S buffer i % 2, once K_i has landed and P_{i-2} V_{i-2} (the last
+      // reader of that buffer) has completed.
+      ok = warp_wait(bar(K_FULL0 + sl), ph, abort_flag, p.status) &&
+           (i < 2 || warp_wait(bar(PV_DONE0 + sl), ph ^ 1u, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint64_t kd = dK + (uint64_t)sl * kSlotStep;
+        const uint32_t tS = tmem + (uint32_t)(kKeys * sl);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t off = (uint64_t)(((k >> 2) * kQBox + (k & 3) * 32) >> 4);
+          const uint64_t offk = (uint64_t)(((k >> 2) * kKVBox + (k & 3) * 32) >> 4);
+          mma_ss(tS, dQ + off, kd + offk, idS, k > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(S_FULL0 + sl));
+        mma_commit(bar(K_EMPTY0 + sl));
+      }
+      __syncwarp();
+    }
     if (lane == 0) {
-      mma_commit(bar(DRAIN));
-      mbar_wait_quiet(bar(DRAIN), 0);
+      // Every MMA of this thread has completed once DRAIN_S fires; no copy may still be writing
+      // shared memory when the CTA leaves.
+      mma_commit(bar(DRAIN_S));
+      mbar_wait_quiet(bar(DRAIN_S), 0);
+      if (*abort_flag) {
+        if (k_loads0) mbar_wait_quiet(bar(K_FULL0), (uint32_t)(k_loads0 - 1) & 1u);
+        if (k_loads1) mbar_wait_quiet(bar(K_FULL1), (uint32_t)(k_loads1 - 1) & 1u);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPVWarp) {
+    // ------------------------------------------------------------------ P V issue + V ring + Q
+    constexpr uint32_t idO = idesc_bf16(kRows, D, true);
+    constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
+    const uint64_t dV = smem_desc_sw128(sV, kKVBox, 1024);
+    const uint32_t tO = tmem + 128;
+    int v_loads0 = 0, v_loads1 = 0;
+    if (lane == 0) {
+      for (int t = 0; t < 2 && t < ntiles; ++t) {
+        load_kv_tile<D>(sV + t * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + t), sTiles[t], h, b);
+        if (t) ++v_loads1; else ++v_loads0;
+      }
+    }
+    bool ok = true;
+    for (int i = 0; i < ntiles; ++i) {
+      // O += P_i V_i
+      const int sl = i & 1;
+      const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+      ok = warp_wait(bar(P_FULL0 + sl), ph, abort_flag, p.status) &&
+           warp_wait(bar(V_FULL0 + sl), ph, abort_flag, p.status);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint64_t vd = dV + (uint64_t)sl * kSlotStep;
+        const uint32_t tP = tmem + (uint32_t)(kKeys * sl);
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k)
+          mma_ts(tO, tP + (uint32_t)(8 * k), vd + (uint64_t)((k * 16 * 128) >> 4), idO,
+                 (i > 0 || k > 0) ? 1u : 0u);
+        mma_commit(bar(PV_DONE0 + sl));
+      }
+      __syncwarp();
+      if (i + 2 < ntiles) {
+        // V slot i % 2 is free once P_i V_i has completed.
+        ok = warp_wait(bar(PV_DONE0 + sl), ph, abort_flag, p.status);
+        if (!ok) break;
+        if (lane == 0) {
+          load_kv_tile<D>(sV + sl * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + sl), sTiles[i + 2], h, b);
+          if (sl) ++v_loads1; else ++v_loads0;
+        }
+      }
+    }
+    if (lane == 0) {
+      mma_commit(bar(DRAIN_PV));
+      mbar_wait_quiet(bar(DRAIN_PV), 0);
+      if (*abort_flag) {
+        mbar_wait_quiet(bar(Q_FULL), 0);
+        if (v_loads0) mbar_wait_quiet(bar(V_FULL0), (uint32_t)(v_loads0 - 1) & 1u);
+        if (v_loads1) mbar_wait_quiet(bar(V_FULL1), (uint32_t)(v_loads1 - 1) & 1u);
+      }
     }
     __syncwarp();
   } else {
