@@ -512,19 +512,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint64_t acc[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[j] = 0ull;
-      uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
+          const uint64_t x2 =
+              f2_fma(f2_pack(__uint_as_float(s[c][j]), __uint_as_float(s[c][j + 1])), kmul2, negm2);
           float x0, x1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c][j]), __uint_as_float(s[c][j + 1])), kmul2,
-                           negm2),
-                    x0, x1);
+          f2_unpack(x2, x0, x1);
           const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
           acc[(j >> 1) & 3] = f2_add(acc[(j >> 1) & 3], f2_pack(p0, p1));
-          pk[c * 16 + j / 2] = pack_bf16(p0, p1);
+          pk[j / 2] = pack_bf16(p0, p1);
         }
+        tmem_st16(tSr + 16 * c, pk);  // P (BF16 pairs) over the first 32 columns of the buffer
       }
       {
         const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
@@ -532,7 +533,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         f2_unpack(f2_add(a01, a23), lo, hi);
         l_run += lo + hi;
       }
-      tmem_st32(tSr, pk);  // P (BF16 pairs) over the first 32 columns of this S buffer
       if (__any_sync(0xffffffffu, need)) {
         // O may only be touched once every P V issued so far (up to tile i-1) has completed;
         // P_i V_i is not issued before this warp arrives on P_FULL below.
