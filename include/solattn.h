@@ -61,15 +61,16 @@ SOLATTN_API const char* solattn_strerror(int code);
 /*
  * Scratch layout of one forward call.  Replaces the torch.empty allocations of the
  * reference launcher (kernels.py:185-190, 203-217): kc/vc (BF16 K/V block means), qc (FP32
- * Q block means), mean/var (FP32 key moments), cutoff (FP32 Eq. 15 thresholds) and one
- * device status word.  Offsets are in bytes from the workspace base, each 256-byte aligned.
- * The pooled tensors use the layout [B, H, blocks, D]; cutoff is [B, H, nqb].
+ * Q block means), mean/var (FP32 key moments), cutoff (FP32 Eq. 15 thresholds), one device
+ * status word, and masks (the routing decisions, uint32 bitmask [B, H, nqb, ceil(nkb/32)]).
+ * Offsets are in bytes from the workspace base, each 256-byte aligned.  The pooled tensors
+ * use the layout [B, H, blocks, D]; cutoff is [B, H, nqb].
  * Returns the total size in bytes, or 0 on an invalid shape.
  */
 SOLATTN_API int64_t solattn_workspace_layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
                                  int64_t* off_kc, int64_t* off_vc, int64_t* off_qc,
                                  int64_t* off_mean, int64_t* off_var, int64_t* off_cutoff,
-                                 int64_t* off_status);
+                                 int64_t* off_status, int64_t* off_masks);
 
 /*
  * Block pooling of Q, K and V in one launch.  Replaces `_pooled`/`_pool`
@@ -112,9 +113,10 @@ SOLATTN_API int solattn_threshold(const void* kc, const float* qc, int64_t B, in
  * (BF16 QK and PV, FP32 online softmax) and folds every unselected block in through its
  * centroid (logit q.kc*scale + log(len), value vc).  cutoff and qc may be NULL when
  * force != 0.  counts may be NULL.  status may be NULL.
- * debug_mask (NULL in normal use) receives the kernel's own routing decisions as a bitmask
- * [B, H, nqb, ceil(nkb/32)] of uint32 words (bit kb%32 of word kb/32 set = block kb exact);
- * it exists only so tests can compare routing bit for bit and is never written otherwise.
+ * masks receives the routing decisions as a bitmask [B, H, nqb, ceil(nkb/32)] of uint32
+ * words (bit kb%32 of word kb/32 set = block kb exact); the call writes it in a routing pass
+ * and the attention kernel reads it back.  It is required when force == SOLATTN_FORCE_THRESHOLD
+ * and may be NULL in the force modes (the rules are then evaluated inside the kernel).
  */
 SOLATTN_API int solattn_attention(const void* q, const void* k, const void* v,
                       int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
@@ -125,7 +127,7 @@ SOLATTN_API int solattn_attention(const void* q, const void* k, const void* v,
                       const void* kc, const void* vc, const float* qc, const float* cutoff,
                       const uint8_t* protect, float scale, int force, int local,
                       int kv_sink_blocks, int q_sink_blocks, void* out, int32_t* counts,
-                      int32_t* status, uint32_t* debug_mask, void* stream);
+                      int32_t* status, uint32_t* masks, void* stream);
 
 /*
  * All-in SOL forward: pool -> threshold (force == 0 only) -> fused attention, the whole of

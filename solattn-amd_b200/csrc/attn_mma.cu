@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
     const uint32_t bal = __ballot_sync(0xffffffffu, sel);
     if (lane == 0) {
       sMask[w] = bal;
-      if (p.debug_mask) p.debug_mask[((int64_t)bh * p.nqb + qb) * nwords + w] = bal;
+      if (p.masks) p.masks[((int64_t)bh * p.nqb + qb) * nwords + w] = bal;
     }
   }
   __syncthreads();

@@ -1,30 +1,36 @@
 // Fused routed attention on the Blackwell data path (replaces `_sol`, kernels.py:101-182).
 //
-// One CTA = one 128-row query tile = two 64-row q-blocks (qb0 = 2*x, qb0 + 1) of one (b, h);
-// 192 threads, two CTAs per SM (256 TMEM columns and ~100 KB of shared memory each).
+// One CTA per SM (it allocates all 512 TMEM columns) = one 128-row query tile = two 64-row
+// q-blocks (qb0 = 2*x, qb0 + 1) of one (b, h); 384 threads.
 //
-// Tiles hold 64 keys: one exact key block, or 64 pooled centroids.  The tile list (shared
-// memory, built by warp 0 after routing) holds first every 64-centroid group that still has a
-// block unselected by either q-block (entry -(t + 1)), then every block of the union of both
+// Tiles hold 64 keys: one exact key block, or 64 pooled centroids.  The routing pass
+// (route.cu) has already written every q-block's exact-block bitmask; the tile list (shared
+// memory, built by warp 0) holds first every 64-centroid group that still has a block
+// unselected by either q-block (entry -(t + 1)), then every block of the union of both
 // q-blocks' exact sets in increasing order (entry kb >= 0).  A row whose q-block did not select
 // an exact block sees it as -inf; a centroid whose block is exact for the row's q-block too.
 //
-// Warp roles:
-//   warps 0-3  softmax: warp w owns TMEM lanes / tile rows 32w..32w+31 (warps 0-1 q-block qb0,
-//              warps 2-3 qb0 + 1).  Per tile: wait S_FULL, tcgen05.ld S, mask/bias, FP32 online
-//              softmax with lazy rescaling, P (BF16) written over its S buffer, arrive P_FULL.
-//              A warp whose q-block does not use the tile writes P = 0 without reading S.
-//              Epilogue O / l -> BF16.
-//   warp 4     S issue (the whole warp runs the loop, lane 0 issues): S_i = Q K_i^T into TMEM
-//              buffer i % 2 once P_{i-2} V_{i-2} has freed it; refills the K ring (2 slots)
-//              when S_{i-1} has completed (K_EMPTY).
-//   warp 5     P V issue: O += P_i V_i once the softmax warps have written P_i; loads Q and
-//              refills the V ring when P_i V_i has completed (PV_DONE).
-//   One thread can issue a tcgen05.mma only about every 100 cycles, so S (8 MMAs of N=64 per
-//   tile) and P V (4 MMAs of N=D) come from two threads; the tensor core works on S_{i+1} and
-//   P_{i-1} V_{i-1} while the softmax warps work on tile i.
-// TMEM: S buffers at columns [0, 64) and [64, 128) (P packed into the first 32 columns of its
-// buffer), O at [128, 128 + D).
+// Two independent online softmaxes run side by side: group g (softmax warps 4g..4g+3) takes
+// the tiles i with i % 2 == g into its own accumulator O_g with its own running max and sum;
+// the epilogue merges the two.  The two warps that share an SM sub-partition therefore work on
+// different tiles and overlap, instead of waiting on each other.
+//
+// TMEM (512 columns): O_0 at [0, 128), O_1 at [128, 256), and kStages S buffers of 64 columns
+// at [256, 512); P (BF16 pairs) is written over the first 32 columns of its S buffer.
+// Shared memory: Q (TMA, read by every S MMA), K and V rings of kStages 64-row tiles each.
+//
+// Warp roles (tile i uses ring slot / S buffer i % kStages):
+//   warps 0-7  softmax: warp w owns TMEM lanes 32(w%4)..+31 for the tiles of group w/4.  Per
+//              tile: tcgen05.ld S, mask/bias, FP32 online softmax with lazy rescaling, P
+//              written over the S buffer, arrive P_FULL.  A warp whose q-block does not use
+//              the tile writes P = 0 without reading S.  Epilogue: merge O_0 and O_1 -> BF16.
+//   warps 8-9  S issue for even / odd tiles (lane 0 issues; the whole warp runs the loop so
+//              that addresses stay warp-uniform): S_i = Q K_i^T once P_{i-kStages} V has freed
+//              the buffer and K_i has landed.  One thread issues a dependent tcgen05.mma about
+//              every 100 cycles; two issuers keep the 8 MMAs (N = 64) per tile flowing.
+//   warp 10    P V issue: O_{i%2} += P_i V_i once the group's four warps have written P_i.
+//   warp 11    TMA producer: Q once, then the K ring (slot refilled when S has completed) and
+//              the V ring (slot refilled when P V has completed).
 #include <cudaTypedefs.h>
 
 #include "sm100.cuh"
@@ -37,21 +43,25 @@ using namespace sm100;
 
 constexpr int kRows = 128;         // query rows per CTA
 constexpr int kKeys = 64;          // keys per tile
-constexpr int kSoftmaxWarps = 4;
-constexpr int kSWarp = 4;   // S = Q K^T issue and the K ring
-constexpr int kPVWarp = 5;  // O += P V issue, the V ring and Q
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+constexpr int kStages = 4;         // S buffers = K slots = V slots
+constexpr int kGroupWarps = 4;     // softmax warps per group (one per TMEM lane quarter)
+constexpr int kSWarp0 = 8;         // S issue, even tiles (kSWarp0 + 1: odd tiles)
+constexpr int kPVWarp = 10;        // P V issue
+constexpr int kKWarp = 11;         // TMA producer: Q and the K and V rings
+constexpr int kThreads = 384;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = 0, kTmemS = 256;  // O_g at kTmemO + 128 g
 constexpr int kQBox = kRows * 128;   // one 128-row x 64-column BF16 box of Q (16 KB)
 constexpr int kKVBox = kKeys * 128;  // one 64-row x 64-column BF16 box of K or V (8 KB)
 constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
 
-// Barriers: slot-indexed pairs for the 2-deep rings.
+// Barriers; ring barriers are indexed by slot.
 enum Bar {
   Q_FULL,
-  K_FULL0, K_FULL1, K_EMPTY0, K_EMPTY1, V_FULL0, V_FULL1,
-  S_FULL0, S_FULL1, P_FULL0, P_FULL1, PV_DONE0, PV_DONE1,
-  DRAIN_S, DRAIN_PV, NBARS
+  K_FULL, K_EMPTY = K_FULL + kStages, V_FULL = K_EMPTY + kStages, S_FULL = V_FULL + kStages,
+  P_FULL = S_FULL + kStages, PV_DONE = P_FULL + kStages,
+  MERGE = PV_DONE + kStages,  // [4 lane quarters], two arrivals each: the epilogue exchange
+  DRAIN_S0 = MERGE + 4, DRAIN_S1, DRAIN_PV, NBARS
 };
 
 template <int D>
@@ -59,19 +69,17 @@ struct Layout {
   static constexpr int kQTile = kRows * D * 2;   // 128 x D BF16
   static constexpr int kKVTile = kKeys * D * 2;  // 64 x D BF16
   static constexpr int kQ = 0;
-  static constexpr int kK = kQTile;                 // 2 slots
-  static constexpr int kV = kK + 2 * kKVTile;       // 2 slots
-  static constexpr int kBars = kV + 2 * kKVTile;
+  static constexpr int kK = kQTile;
+  static constexpr int kV = kK + kStages * kKVTile;
+  static constexpr int kBars = kV + kStages * kKVTile;
   static constexpr int kMisc = kBars + NBARS * 8;   // [0] TMEM address [1] abort [2] tiles
-  static constexpr int kQbar = kMisc + 16;          // float [2][D]
-  static constexpr int kMask = kQbar + 2 * D * 4;   // uint32 [2][nwords]
+  static constexpr int kMerge = kMisc + 16;         // float [8 warps][2][32 lanes]: m, l
+  static constexpr int kMask = kMerge + 8 * 2 * 32 * 4;  // uint32 [2][nwords]
   __host__ __device__ static int tiles_offset(int nwords) { return kMask + 2 * nwords * 4; }  // int16
   __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + nkb; }
   static size_t bytes(int nkb) {
     const int nwords = (nkb + 31) / 32;
-    size_t n = 1024 + (size_t)tiles_offset(nwords) + (size_t)max_tiles(nkb) * 2;
-    // At most two CTAs per SM: each holds 256 of the SM's 512 TMEM columns.
-    return n < 80 * 1024 ? 80 * 1024 : n;
+    return 1024 + (size_t)tiles_offset(nwords) + (size_t)max_tiles(nkb) * 2;
   }
 };
 
@@ -95,6 +103,11 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
                                           int32_t* status) {
   const bool ok = mbar_wait(bar, parity, abort_flag, status);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Loads issued into ring slot s after `issued` loads in total (loads go to slots 0, 1, ...).
+__device__ __forceinline__ int loads_into(int issued, int s) {
+  return issued > s ? (issued - s + kStages - 1) / kStages : 0;
 }
 
 // TMA loads of one K or V tile (tile-list entry e) into `dst` on barrier `full`: 64 centroid rows
@@ -131,7 +144,7 @@ __device__ __forceinline__ float row_max64(const uint32_t (&s)[2][32]) {
 
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_sm100_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const __grid_constant__ CUtensorMap tmKC,
@@ -146,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto bar = [bar0](int i) { return bar0 + 8u * (uint32_t)i; };
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
-  float* sQbar = reinterpret_cast<float*>(smem + L::kQbar);
+  float* sMerge = reinterpret_cast<float*>(smem + L::kMerge);
   uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + L::kMask);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -160,22 +173,33 @@ __global__ void __launch_bounds__(kThreads, 2)
   int16_t* sTiles = reinterpret_cast<int16_t*>(smem + L::tiles_offset(nwords));
 
   if (tid == 0) {
-    for (int i = 0; i < NBARS; ++i)
-      mbar_init(bar(i), (i == P_FULL0 || i == P_FULL1) ? kSoftmaxWarps : 1);
+    for (int i = 0; i < NBARS; ++i) {
+      uint32_t count = 1;
+      if (i >= P_FULL && i < P_FULL + kStages) count = kGroupWarps;
+      if (i >= MERGE && i < MERGE + 4) count = 2;
+      mbar_init(bar(i), count);
+    }
     misc[1] = 0;
     misc[2] = 0;
     mbar_fence_init();
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(misc), kTmemCols);
-    // Give up the allocation permit at once: while a CTA holds it, no further CTA that needs
-    // TMEM is launched on this SM, and two CTAs per SM are what hides the softmax.
     tmem_relinquish();
   }
-  if (p.force == 0) {
-    for (int i = tid; i < 2 * D; i += kThreads) {
-      const int qb = qb0 + i / D;
-      sQbar[i] = qb < p.nqb ? p.qc[((int64_t)bh * p.nqb + qb) * D + (i % D)] : 0.f;
+  // Both q-blocks' exact-block bitmasks: from the routing pass, or (force modes without a
+  // mask buffer) from the force / local / sink / protected rules alone.
+  if (p.masks) {
+    for (int i = tid; i < 2 * nwords; i += kThreads) {
+      const int qb = qb0 + i / nwords;
+      sMask[i] = qb < p.nqb ? p.masks[((int64_t)bh * p.nqb + qb) * nwords + (i % nwords)] : 0u;
+    }
+  } else {
+    for (int i = warp; i < 2 * nwords; i += kThreads / 32) {
+      const int qb = qb0 + i / nwords, kb = 32 * (i % nwords) + lane;
+      const bool sel = qb < p.nqb && kb < p.nkb && route_rules(p, false, b, qb, kb);
+      const uint32_t bal = __ballot_sync(0xffffffffu, sel);
+      if (lane == 0) sMask[i] = bal;
     }
   }
   tc_fence_before();
@@ -183,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (tid == kPVWarp * 32) {  // Q starts loading before the routing prologue
+  if (tid == kKWarp * 32) {  // Q starts loading at once
     tma_prefetch(&tmQ);
     tma_prefetch(&tmK);
     tma_prefetch(&tmV);
@@ -193,36 +217,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = 0; j < D / 64; ++j)
       tma_load_4d(sQ + j * kQBox, &tmQ, bar(Q_FULL), 64 * j, qb0 * kBlock, h, b);
   }
-
-  // ---- routing of both q-blocks into shared bitmasks ----
-  // Lane kb of a warp reads centroid row kb once and forms both q-blocks' proxies from it (the
-  // arithmetic of common.cuh:route_selected, bit for bit); one ballot per q-block per 32 blocks.
-  const __nv_bfloat16* kc_bh = p.kc + (int64_t)bh * p.nkb * D;
-  for (int wi = warp; wi < nwords; wi += kThreads / 32) {
-    const int kb = wi * 32 + lane;
-    const int kbc = kb < p.nkb ? kb : p.nkb - 1;  // clamped: every address stays in range
-    bool sel[2] = {false, false};
-    if (p.force == 0) {
-      float d0, d1;
-      routing_dot2(sQbar, sQbar + D, kc_bh + (int64_t)kbc * D, D, d0, d1);
-      const float cut0 = p.cutoff[(int64_t)bh * p.nqb + qb0];
-      const float cut1 = has1 ? p.cutoff[(int64_t)bh * p.nqb + qb0 + 1] : 0.f;
-      sel[0] = __fmul_rn(d0, p.scale) > cut0;
-      sel[1] = __fmul_rn(d1, p.scale) > cut1;
-    }
-#pragma unroll
-    for (int qsel = 0; qsel < 2; ++qsel) {
-      const int qb = qb0 + qsel;
-      bool s_ = false;
-      if (kb < p.nkb && qb < p.nqb) s_ = route_rules(p, sel[qsel], b, qb, kb);
-      const uint32_t bal = __ballot_sync(0xffffffffu, s_);
-      if (lane == 0) {
-        sMask[qsel * nwords + wi] = bal;
-        if (p.debug_mask && qb < p.nqb) p.debug_mask[((int64_t)bh * p.nqb + qb) * nwords + wi] = bal;
-      }
-    }
-  }
-  __syncthreads();
 
   // ---- tile list (warp 0) and exact-block counts ----
   if (warp == 0) {
@@ -236,8 +230,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (t < nct) {
         for (int wi = 2 * t; wi < 2 * t + 2 && wi < nwords; ++wi) {
           const uint32_t v = valid_word(wi, p.nkb);
-          const uint32_t w0 = m0[wi], w1 = m1[wi];
-          if ((~w0 & v) || (has1 && (~w1 & v))) useful = true;
+          if ((~m0[wi] & v) || (has1 && (~m1[wi] & v))) useful = true;
         }
       }
       const uint32_t bal = __ballot_sync(0xffffffffu, useful);
@@ -274,126 +267,108 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   const int ntiles = (int)misc[2];
 
-  if (warp == kSWarp) {
-    // ------------------------------------------------------------------ S issue + K ring
-    // The whole warp runs the loop so that descriptors and addresses stay warp-uniform; lane 0
-    // issues every copy, MMA and commit (a commit tracks the MMAs of its own thread).  S and
-    // P V are issued by two different warps: one thread can issue a tcgen05.mma only every
-    // ~100 cycles, more than an M=128 N=64 MMA computes.
-    constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
-    constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
-    const uint64_t dQ = smem_desc_sw128(sQ, 16, 1024);
-    const uint64_t dK = smem_desc_sw128(sK, 16, 1024);
-    int k_loads0 = 0, k_loads1 = 0;  // copies issued per slot (for the drain after an abort)
+  if (warp == kKWarp) {
+    // ------------------------------------------------------------------ TMA producer: K, V rings
+    // Slot s of the K ring is free once S_{i - kStages} has completed, slot s of the V ring once
+    // P_{i - kStages} V_{i - kStages} has; S_i itself waits for the latter, so loading K_i
+    // before that wait delays nothing.
     if (lane == 0) {
-      for (int t = 0; t < 2 && t < ntiles; ++t) {
-        load_kv_tile<D>(sK + t * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + t), sTiles[t], h, b);
-        if (t) ++k_loads1; else ++k_loads0;
+      int k_issued = 0, v_issued = 0;
+      for (int i = 0; i < ntiles; ++i) {
+        const int s = i % kStages;
+        const uint32_t prev = (uint32_t)(i / kStages - 1) & 1u;  // parity of the slot's last use
+        if (i >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) break;
+        load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), sTiles[i], h, b);
+        ++k_issued;
+        if (i >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) break;
+        load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), sTiles[i], h, b);
+        ++v_issued;
       }
-    }
-    bool ok = warp_wait(bar(Q_FULL), 0, abort_flag, p.status);
-    for (int i = 0; ok && i < ntiles; ++i) {
-      const int sl = i & 1;
-      const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-      if (i >= 1 && i + 1 < ntiles) {
-        // K slot (i + 1) % 2 is free once S_{i-1} has completed.
-        const int fs = (i - 1) & 1;
-        ok = warp_wait(bar(K_EMPTY0 + fs), (uint32_t)((i - 1) >> 1) & 1u, abort_flag, p.status);
-        if (!ok) break;
-        if (lane == 0) {
-          load_kv_tile<D>(sK + fs * L::kKVTile, &tmK, &tmKC, bar(K_FULL0 + fs), sTiles[i + 1], h, b);
-          if (fs) ++k_loads1; else ++k_loads0;
+      if (*abort_flag) {  // never leave while a bulk copy may still write shared memory
+        mbar_wait_quiet(bar(Q_FULL), 0);
+        for (int s = 0; s < kStages; ++s) {
+          int n = loads_into(k_issued, s);
+          if (n) mbar_wait_quiet(bar(K_FULL + s), (uint32_t)(n - 1) & 1u);
+          n = loads_into(v_issued, s);
+          if (n) mbar_wait_quiet(bar(V_FULL + s), (uint32_t)(n - 1) & 1u);
         }
-      }
-      // S_i = Q K_i^T into S buffer i % 2, once K_i has landed and P_{i-2} V_{i-2} (the last
-      // reader of that buffer) has completed.
-      ok = warp_wait(bar(K_FULL0 + sl), ph, abort_flag, p.status) &&
-           (i < 2 || warp_wait(bar(PV_DONE0 + sl), ph ^ 1u, abort_flag, p.status));
-      if (!ok) break;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint64_t kd = dK + (uint64_t)sl * kSlotStep;
-        const uint32_t tS = tmem + (uint32_t)(kKeys * sl);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint64_t off = (uint64_t)(((k >> 2) * kQBox + (k & 3) * 32) >> 4);
-          const uint64_t offk = (uint64_t)(((k >> 2) * kKVBox + (k & 3) * 32) >> 4);
-          mma_ss(tS, dQ + off, kd + offk, idS, k > 0 ? 1u : 0u);
-        }
-        mma_commit(bar(S_FULL0 + sl));
-        mma_commit(bar(K_EMPTY0 + sl));
-      }
-      __syncwarp();
-    }
-    if (lane == 0) {
-      // Every MMA of this thread has completed once DRAIN_S fires; no copy may still be writing
-      // shared memory when the CTA leaves.
-      mma_commit(bar(DRAIN_S));
-      mbar_wait_quiet(bar(DRAIN_S), 0);
-      if (*abort_flag) {
-        if (k_loads0) mbar_wait_quiet(bar(K_FULL0), (uint32_t)(k_loads0 - 1) & 1u);
-        if (k_loads1) mbar_wait_quiet(bar(K_FULL1), (uint32_t)(k_loads1 - 1) & 1u);
       }
     }
     __syncwarp();
   } else if (warp == kPVWarp) {
-    // ------------------------------------------------------------------ P V issue + V ring + Q
+    // ------------------------------------------------------------------ P V issue
     constexpr uint32_t idO = idesc_bf16(kRows, D, true);
     constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
     const uint64_t dV = smem_desc_sw128(sV, kKVBox, 1024);
-    const uint32_t tO = tmem + 128;
-    int v_loads0 = 0, v_loads1 = 0;
-    if (lane == 0) {
-      for (int t = 0; t < 2 && t < ntiles; ++t) {
-        load_kv_tile<D>(sV + t * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + t), sTiles[t], h, b);
-        if (t) ++v_loads1; else ++v_loads0;
-      }
-    }
-    bool ok = true;
     for (int i = 0; i < ntiles; ++i) {
-      // O += P_i V_i
-      const int sl = i & 1;
-      const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-      ok = warp_wait(bar(P_FULL0 + sl), ph, abort_flag, p.status) &&
-           warp_wait(bar(V_FULL0 + sl), ph, abort_flag, p.status);
-      if (!ok) break;
+      const int s = i % kStages;
+      const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+      if (!warp_wait(bar(P_FULL + s), ph, abort_flag, p.status) ||
+          !warp_wait(bar(V_FULL + s), ph, abort_flag, p.status))
+        break;
       tc_fence_after();
       if (lane == 0) {
-        const uint64_t vd = dV + (uint64_t)sl * kSlotStep;
-        const uint32_t tP = tmem + (uint32_t)(kKeys * sl);
+        const uint64_t vd = dV + (uint64_t)s * kSlotStep;
+        const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
+        const uint32_t tO = tmem + kTmemO + (uint32_t)(128 * (i & 1));  // the tile's group
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k)
           mma_ts(tO, tP + (uint32_t)(8 * k), vd + (uint64_t)((k * 16 * 128) >> 4), idO,
-                 (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit(bar(PV_DONE0 + sl));
+                 (i > 1 || k > 0) ? 1u : 0u);
+        mma_commit(bar(PV_DONE + s));
       }
       __syncwarp();
-      if (i + 2 < ntiles) {
-        // V slot i % 2 is free once P_i V_i has completed.
-        ok = warp_wait(bar(PV_DONE0 + sl), ph, abort_flag, p.status);
-        if (!ok) break;
-        if (lane == 0) {
-          load_kv_tile<D>(sV + sl * L::kKVTile, &tmV, &tmVC, bar(V_FULL0 + sl), sTiles[i + 2], h, b);
-          if (sl) ++v_loads1; else ++v_loads0;
-        }
-      }
     }
     if (lane == 0) {
       mma_commit(bar(DRAIN_PV));
       mbar_wait_quiet(bar(DRAIN_PV), 0);
-      if (*abort_flag) {
-        mbar_wait_quiet(bar(Q_FULL), 0);
-        if (v_loads0) mbar_wait_quiet(bar(V_FULL0), (uint32_t)(v_loads0 - 1) & 1u);
-        if (v_loads1) mbar_wait_quiet(bar(V_FULL1), (uint32_t)(v_loads1 - 1) & 1u);
+    }
+    __syncwarp();
+  } else if (warp >= kSWarp0) {
+    // ------------------------------------------------------------------ S issue (two warps)
+    const int par = warp - kSWarp0;  // tiles i with i % 2 == par
+    constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
+    constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
+    const uint64_t dQ = smem_desc_sw128(sQ, 16, 1024);
+    const uint64_t dK = smem_desc_sw128(sK, 16, 1024);
+    if (warp_wait(bar(Q_FULL), 0, abort_flag, p.status)) {
+      for (int i = par; i < ntiles; i += 2) {
+        const int s = i % kStages;
+        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        // P_{i - kStages} V_{i - kStages} (the last reader of the buffer) has completed, and
+        // K_i has landed.  The order matters: the two issuers run independently, and only once
+        // tile i - kStages is finished can K_FULL of this slot not still be a phase behind
+        // (a parity wait on a barrier two phases behind would pass at once).
+        if (i >= kStages && !warp_wait(bar(PV_DONE + s), ph ^ 1u, abort_flag, p.status)) break;
+        if (!warp_wait(bar(K_FULL + s), ph, abort_flag, p.status)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t kd = dK + (uint64_t)s * kSlotStep;
+          const uint32_t tS = tmem + kTmemS + (uint32_t)(kKeys * s);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t off = (uint64_t)(((k >> 2) * kQBox + (k & 3) * 32) >> 4);
+            const uint64_t offk = (uint64_t)(((k >> 2) * kKVBox + (k & 3) * 32) >> 4);
+            mma_ss(tS, dQ + off, kd + offk, idS, k > 0 ? 1u : 0u);
+          }
+          mma_commit(bar(S_FULL + s));
+          mma_commit(bar(K_EMPTY + s));
+        }
+        __syncwarp();
       }
+    }
+    if (lane == 0) {
+      mma_commit(bar(DRAIN_S0 + par));
+      mbar_wait_quiet(bar(DRAIN_S0 + par), 0);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax warps
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;  // warp w reads TMEM lanes 32w..
-    const uint32_t tOr = tmem + 128 + lane_base;
-    const int row = warp * 32 + lane;
-    const int qsel = warp >> 1;                    // warps 0-1: qb0, warps 2-3: qb0 + 1
+    const int quarter = warp & 3, grp = warp >> 2;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;  // TMEM lanes 32 quarter..
+    const uint32_t tOr = tmem + kTmemO + (uint32_t)(128 * grp) + lane_base;
+    const int row = quarter * 32 + lane;
+    const int qsel = quarter >> 1;                 // lanes 0-63: qb0, lanes 64-127: qb0 + 1
     const bool warp_rows = qsel == 0 || has1;      // the warp's q-block exists
     const uint32_t* mymask = sMask + qsel * nwords;
     const float sl2 = p.scale_log2;
@@ -404,10 +379,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int last_col = (p.nkb - 1) & 63;         // column of the last centroid in its group
     const int last_group = (p.nkb - 1) >> 6;
     float m_run = -INFINITY, l_run = 0.f;
-    int i = 0;
     bool ok = true;
-    for (; i < ntiles; ++i) {
-      const int sl = i & 1;
+    int last = -1;  // this group's previous tile (its P V is the last one into O_grp)
+    for (int i = grp; ok && i < ntiles; i += 2) {
+      const int s = i % kStages;
       // Tile metadata first: these shared-memory reads overlap the wait for S.  Every value
       // below is warp-uniform (one q-block per warp).
       const int entry = sTiles[i];
@@ -424,12 +399,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         len = min(kBlock, p.Tk - entry * kBlock);
       }
       const bool active = centroid ? (approx0 | approx1) != 0u : len > 0;
-      if (!warp_wait(bar(S_FULL0 + sl), (uint32_t)(i >> 1) & 1u, abort_flag, p.status)) {
+      if (!warp_wait(bar(S_FULL + s), (uint32_t)(i / kStages) & 1u, abort_flag, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t tSr = tmem + (uint32_t)(kKeys * sl) + lane_base;
+      const uint32_t tSr = tmem + kTmemS + (uint32_t)(kKeys * s) + lane_base;
       if (!active) {
         // The tile contributes nothing to these rows: P = 0, the running max and sum stay.
         uint32_t z[32];
@@ -439,12 +414,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(P_FULL0 + sl));
+        if (lane == 0) mbar_arrive(bar(P_FULL + s));
+        last = i;
         continue;
       }
-      uint32_t s[2][32];
-      tmem_ld32(tSr, s[0]);
-      tmem_ld32(tSr + 32, s[1]);
+      uint32_t sv[2][32];
+      tmem_ld32(tSr, sv[0]);
+      tmem_ld32(tSr + 32, sv[1]);
       tmem_wait_ld();
       float m_tile, k_mul;
       if (centroid) {
@@ -458,9 +434,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float bias = (32 * c + j) == last_col ? last_bias : 6.f;
-              const float v = ((approx >> j) & 1u) ? fmaf(__uint_as_float(s[c][j]), sl2, bias)
+              const float v = ((approx >> j) & 1u) ? fmaf(__uint_as_float(sv[c][j]), sl2, bias)
                                                    : -INFINITY;
-              s[c][j] = __float_as_uint(v);
+              sv[c][j] = __float_as_uint(v);
             }
           }
         } else {
@@ -470,15 +446,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
               float v0, v1;
-              f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c][j]), __uint_as_float(s[c][j + 1])),
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][j]), __uint_as_float(sv[c][j + 1])),
                                sl2x2, six2),
                         v0, v1);
-              s[c][j] = __float_as_uint(((approx >> j) & 1u) ? v0 : -INFINITY);
-              s[c][j + 1] = __float_as_uint(((approx >> (j + 1)) & 1u) ? v1 : -INFINITY);
+              sv[c][j] = __float_as_uint(((approx >> j) & 1u) ? v0 : -INFINITY);
+              sv[c][j + 1] = __float_as_uint(((approx >> (j + 1)) & 1u) ? v1 : -INFINITY);
             }
           }
         }
-        m_tile = row_max64(s);
+        m_tile = row_max64(sv);
         k_mul = 1.f;
       } else {
         // Exact tiles keep raw scores: max(s) * scale_log2 equals max(s * scale_log2) bit for
@@ -488,9 +464,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (32 * c + j >= len) s[c][j] = __float_as_uint(-INFINITY);
+              if (32 * c + j >= len) sv[c][j] = __float_as_uint(-INFINITY);
         }
-        m_tile = row_max64(s) * sl2;
+        m_tile = row_max64(sv) * sl2;
         k_mul = sl2;
       }
       // Lazy rescaling: the running max only moves when a row's max grows by more than 8
@@ -517,15 +493,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const uint64_t x2 =
-              f2_fma(f2_pack(__uint_as_float(s[c][j]), __uint_as_float(s[c][j + 1])), kmul2, negm2);
           float x0, x1;
-          f2_unpack(x2, x0, x1);
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][j]), __uint_as_float(sv[c][j + 1])),
+                           kmul2, negm2),
+                    x0, x1);
           const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
           acc[(j >> 1) & 3] = f2_add(acc[(j >> 1) & 3], f2_pack(p0, p1));
           pk[j / 2] = pack_bf16(p0, p1);
         }
-        tmem_st16(tSr + 16 * c, pk);  // P (BF16 pairs) over the first 32 columns of the buffer
+        tmem_st16(tSr + (uint32_t)(16 * c), pk);  // P over the first 32 columns of the buffer
       }
       {
         const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
@@ -534,10 +510,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         l_run += lo + hi;
       }
       if (__any_sync(0xffffffffu, need)) {
-        // O may only be touched once every P V issued so far (up to tile i-1) has completed;
-        // P_i V_i is not issued before this warp arrives on P_FULL below.
-        if (!warp_wait(bar(PV_DONE0 + ((i - 1) & 1)), (uint32_t)((i - 1) >> 1) & 1u, abort_flag,
-                       p.status)) {
+        // O_grp may only be touched once the group's previous P V has completed (the P V issue
+        // is in order); P_i V_i is not issued before this group arrives on P_FULL below.
+        if (!warp_wait(bar(PV_DONE + last % kStages), (uint32_t)(last / kStages) & 1u,
+                       abort_flag, p.status)) {
           tmem_wait_st();
           ok = false;
           break;
@@ -551,10 +527,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            float x0, x1;
-            f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), a2), x0, x1);
-            o[j] = __float_as_uint(x0);
-            o[j + 1] = __float_as_uint(x1);
+            float y0, y1;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), a2), y0, y1);
+            o[j] = __float_as_uint(y0);
+            o[j + 1] = __float_as_uint(y1);
           }
           tmem_st32(tOr + 32 * c, o);
         }
@@ -562,27 +538,59 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(P_FULL0 + sl));
+      if (lane == 0) mbar_arrive(bar(P_FULL + s));
+      last = i;
     }
-    // ---- epilogue: O / l -> BF16 ----
-    if (ok && ntiles > 0 &&
-        warp_wait(bar(PV_DONE0 + ((ntiles - 1) & 1)), (uint32_t)((ntiles - 1) >> 1) & 1u,
-                  abort_flag, p.status)) {
+    // ---- epilogue: merge the two groups' softmaxes, O / l -> BF16 ----
+    if (ok && last >= 0)
+      ok = warp_wait(bar(PV_DONE + last % kStages), (uint32_t)(last / kStages) & 1u, abort_flag,
+                     p.status);
+    const float m_me = last >= 0 ? m_run : -INFINITY;
+    if (ok) {  // the partner warp (same lanes, other group) is warp ^ 4
+      sMerge[(warp * 2) * 32 + lane] = m_me;
+      sMerge[(warp * 2 + 1) * 32 + lane] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(MERGE + quarter));
+      ok = warp_wait(bar(MERGE + quarter), 0, abort_flag, p.status);
+    }
+    if (ok) {
       tc_fence_after();
-      const float inv = 1.f / l_run;
+      const float m_o = sMerge[((warp ^ 4) * 2) * 32 + lane];
+      const float l_o = sMerge[((warp ^ 4) * 2 + 1) * 32 + lane];
+      const float m0 = grp == 0 ? m_me : m_o, m1 = grp == 0 ? m_o : m_me;
+      const float l0 = grp == 0 ? l_run : l_o, l1 = grp == 0 ? l_o : l_run;
+      const float m = fmaxf(m0, m1);
+      const float f0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
+      const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
+      const float inv = 1.f / (l0 * f0 + l1 * f1);
+      // A group without tiles never initialised its accumulator: its share is skipped.
+      const bool has0 = ntiles >= 1, has1t = ntiles >= 2;
       const int grow = qb0 * kBlock + row;
-      __nv_bfloat16* dst = p.out + (((int64_t)b * p.Tq + grow) * p.H + h) * D;
+      // This warp writes head dims [grp * D / 2, (grp + 1) * D / 2) of its 32 rows.
+      __nv_bfloat16* dst = p.out + (((int64_t)b * p.Tq + grow) * p.H + h) * D + grp * (D / 2);
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tOr + 32 * c, o);
+      for (int c = 0; c < D / 64; ++c) {
+        const uint32_t col = (uint32_t)(grp * (D / 2) + 32 * c);
+        uint32_t o0[32], o1[32];
+        if (has0) tmem_ld32(tmem + kTmemO + lane_base + col, o0);
+        if (has1t) tmem_ld32(tmem + kTmemO + 128 + lane_base + col, o1);
         tmem_wait_ld();
         if (grow < p.Tq) {
           uint4 v4[4];
           uint32_t* w32 = reinterpret_cast<uint32_t*>(v4);
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            w32[j] = pack_bf16(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+          for (int j = 0; j < 16; ++j) {
+            float a0 = 0.f, a1 = 0.f;
+            if (has0) {
+              a0 = __uint_as_float(o0[2 * j]) * f0;
+              a1 = __uint_as_float(o0[2 * j + 1]) * f0;
+            }
+            if (has1t) {
+              a0 = fmaf(__uint_as_float(o1[2 * j]), f1, a0);
+              a1 = fmaf(__uint_as_float(o1[2 * j + 1]), f1, a1);
+            }
+            w32[j] = pack_bf16(a0 * inv, a1 * inv);
+          }
           uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
 #pragma unroll
           for (int j = 0; j < 4; ++j) d4[j] = v4[j];
@@ -600,6 +608,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // ---------------------------------------------------------------- host side
+cudaError_t launch_route(const AttnParams& p, int D, cudaStream_t stream);  // route.cu
+
 namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -649,7 +659,7 @@ bool make_pooled_map(CUtensorMap* map, const __nv_bfloat16* base, int B, int H, 
 
 template <int D>
 cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
-  if (p.nkb > kMaxKeyBlocks) return cudaErrorInvalidValue;
+  if (p.nkb > kMaxKeyBlocks || (p.masks == nullptr && p.force == 0)) return cudaErrorInvalidValue;
   CUtensorMap tmQ, tmK, tmV, tmKC, tmVC;
   if (!make_bthd_map(&tmQ, p.q, p.B, p.Tq, p.H, D, kRows) ||
       !make_bthd_map(&tmK, p.k, p.B, p.Tk, p.H, D, kBlock) ||
@@ -657,9 +667,14 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
       !make_pooled_map(&tmKC, p.kc, p.B, p.H, p.nkb, D) ||
       !make_pooled_map(&tmVC, p.vc, p.B, p.H, p.nkb, D))
     return cudaErrorInvalidValue;
+  cudaError_t err = cudaSuccess;
+  if (p.masks) {
+    err = launch_route(p, D, stream);
+    if (err != cudaSuccess) return err;
+  }
   const size_t smem = Layout<D>::bytes(p.nkb);
-  cudaError_t err = cudaFuncSetAttribute(attn_sm100_kernel<D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  err = cudaFuncSetAttribute(attn_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
   if (err != cudaSuccess) return err;
   dim3 grid((p.nqb + 1) / 2, p.B * p.H);
   attn_sm100_kernel<D><<<grid, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
@@ -671,7 +686,7 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
 // The softmax folds a positive scale into the exponent (max(s) * scale == max(s * scale) and
 // masked -inf scores stay -inf), so other scales take the mma.sync kernel.
 bool attn_sm100_supported(const AttnParams& p) {
-  return p.nkb <= kMaxKeyBlocks && p.scale_log2 > 0.f;
+  return p.nkb <= kMaxKeyBlocks && p.scale_log2 > 0.f && (p.masks != nullptr || p.force != 0);
 }
 
 cudaError_t launch_attn_sm100(const AttnParams& p, int D, cudaStream_t stream) {

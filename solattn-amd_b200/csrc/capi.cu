@@ -56,7 +56,7 @@ TensorView view(const void* ptr, int64_t sB, int64_t sT, int64_t sH, const int64
 int from_cuda(cudaError_t e) { return e == cudaSuccess ? SOLATTN_OK : SOLATTN_ERR_LAUNCH; }
 
 struct Layout {
-  int64_t kc, vc, qc, mean, var, cutoff, status, total;
+  int64_t kc, vc, qc, mean, var, cutoff, masks, status, total;
 };
 
 Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
@@ -77,6 +77,8 @@ Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   off = align256(off + B * H * D * 4);
   L.cutoff = off;
   off = align256(off + B * H * nqb * 4);
+  L.masks = off;
+  off = align256(off + B * H * nqb * cdiv(nkb, 32) * 4);
   L.total = off;
   return L;
 }
@@ -106,7 +108,7 @@ const char* solattn_strerror(int code) {
 int64_t solattn_workspace_layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
                                  int64_t* off_kc, int64_t* off_vc, int64_t* off_qc,
                                  int64_t* off_mean, int64_t* off_var, int64_t* off_cutoff,
-                                 int64_t* off_status) {
+                                 int64_t* off_status, int64_t* off_masks) {
   if (check_shapes(B, Tq, Tk, H, D) != SOLATTN_OK) return 0;
   const Layout L = layout(B, Tq, Tk, H, D);
   if (off_kc) *off_kc = L.kc;
@@ -116,6 +118,7 @@ int64_t solattn_workspace_layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, i
   if (off_var) *off_var = L.var;
   if (off_cutoff) *off_cutoff = L.cutoff;
   if (off_status) *off_status = L.status;
+  if (off_masks) *off_masks = L.masks;
   return L.total;
 }
 
@@ -170,10 +173,11 @@ int solattn_attention(const void* q, const void* k, const void* v, int64_t B, in
                       const void* kc, const void* vc, const float* qc, const float* cutoff,
                       const uint8_t* protect, float scale, int force, int local,
                       int kv_sink_blocks, int q_sink_blocks, void* out, int32_t* counts,
-                      int32_t* status, uint32_t* debug_mask, void* stream) {
+                      int32_t* status, uint32_t* masks, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (!q || !k || !v || !kc || !vc || !out) return SOLATTN_ERR_ARG;
+  if (force == SOLATTN_FORCE_THRESHOLD && !masks) return SOLATTN_ERR_ARG;
   if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
   if (force < 0 || force > 2 || (force == 0 && (!qc || !cutoff))) return SOLATTN_ERR_ARG;
   if (!(scale > 0.f) || !isfinite(scale) || kv_sink_blocks < 0 || q_sink_blocks < 0)
@@ -196,7 +200,7 @@ int solattn_attention(const void* q, const void* k, const void* v, int64_t B, in
   p.out = static_cast<__nv_bfloat16*>(out);
   p.counts = counts;
   p.status = status;
-  p.debug_mask = debug_mask;
+  p.masks = masks;
   p.B = (int)B;
   p.Tq = (int)Tq;
   p.Tk = (int)Tk;
@@ -261,7 +265,7 @@ int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, 
                            force == SOLATTN_FORCE_THRESHOLD ? qc : nullptr,
                            force == SOLATTN_FORCE_THRESHOLD ? cutoff : nullptr, protect, scale,
                            force, local, kv_sink_blocks, q_sink_blocks, out, counts, status,
-                           nullptr, stream);
+                           reinterpret_cast<uint32_t*>(ws + L.masks), stream);
 }
 
 int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,

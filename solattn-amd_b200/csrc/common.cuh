@@ -34,7 +34,8 @@ struct AttnParams {
   __nv_bfloat16* out;       // [B, Tq, H, D]
   int32_t* counts;          // [B, nqb, H] or nullptr
   int32_t* status;          // device status word or nullptr
-  uint32_t* debug_mask;     // [B, H, nqb, ceil(nkb/32)] routing bitmask (tests only) or nullptr
+  uint32_t* masks;          // [B, H, nqb, ceil(nkb/32)] routing bitmask: written by route.cu
+                            // (read by attn_sm100_kernel) or by attn_mma_kernel
   int B, Tq, Tk, H, nqb, nkb;
   float scale;       // softmax scale (natural-log units), used by routing
   float scale_log2;  // scale * log2(e), used by the softmax

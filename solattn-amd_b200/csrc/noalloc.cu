@@ -72,7 +72,7 @@ int solattn_sol_forward_noalloc(const void* q, const void* k, const void* v, int
                                 int kv_sink_blocks, int q_sink_blocks, void* out,
                                 int32_t* counts, void* stream) {
   const int64_t need = solattn_workspace_layout(B, Tq, Tk, H, D, nullptr, nullptr, nullptr,
-                                                nullptr, nullptr, nullptr, nullptr);
+                                                nullptr, nullptr, nullptr, nullptr, nullptr);
   if (need <= 0) return (D != 64 && D != 128) ? SOLATTN_ERR_UNSUPPORTED : SOLATTN_ERR_ARG;
   if (need > kNoAllocScratchBytes) return SOLATTN_ERR_TOO_LARGE;
   void* scratch = nullptr;

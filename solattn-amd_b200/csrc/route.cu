@@ -1,0 +1,98 @@
+// Routing pass: the exact-block bitmask of every (b, h, q-block) (kernels.py:130-143,
+// reference.py:41-51), written before the fused attention kernel runs so that the attention
+// CTAs start on their tiles at once.
+//
+// One CTA per (b, h) and group of kRouteQB q-blocks, 256 threads.  Lane kb of a warp reads
+// centroid row kb once (16-byte loads) and forms the proxies of all the group's q-blocks from it,
+// with exactly the arithmetic of common.cuh:routing_dot (eight partial sums over d = 8i + j,
+// __fmul_rn / __fadd_rn, combined pairwise), so the decisions are bit-identical to the
+// per-CTA routing of the mma.sync kernel.  One ballot per q-block per 32 key blocks gives a
+// mask word: masks[((b * H + h) * nqb + qb) * nwords + kb / 32], bit kb % 32.
+#include "common.cuh"
+
+namespace solattn {
+
+namespace {
+
+constexpr int kRouteQB = 8;
+constexpr int kRouteThreads = 256;
+
+template <int D>
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const AttnParams p) {
+  __shared__ float sq[kRouteQB][D];
+  __shared__ float scut[kRouteQB];
+  const int bh = blockIdx.y;
+  const int b = bh / p.H;
+  const int qb_lo = blockIdx.x * kRouteQB;
+  const int nq = min(kRouteQB, p.nqb - qb_lo);
+  const int nwords = (p.nkb + 31) / 32;
+  for (int i = threadIdx.x; i < kRouteQB * D; i += kRouteThreads) {
+    const int j = i / D;
+    sq[j][i % D] =
+        (p.force == 0 && j < nq) ? p.qc[((int64_t)bh * p.nqb + qb_lo + j) * D + (i % D)] : 0.f;
+  }
+  if (threadIdx.x < kRouteQB)
+    scut[threadIdx.x] = (p.force == 0 && (int)threadIdx.x < nq)
+                            ? p.cutoff[(int64_t)bh * p.nqb + qb_lo + threadIdx.x]
+                            : 0.f;
+  __syncthreads();
+
+  const __nv_bfloat16* kc_bh = p.kc + (int64_t)bh * p.nkb * D;
+  const int lane = threadIdx.x & 31;
+  // Warp-uniform loop over 32-block words.
+  for (int w = threadIdx.x >> 5; w < nwords; w += kRouteThreads / 32) {
+    const int kb = 32 * w + lane;
+    const int kbc = kb < p.nkb ? kb : p.nkb - 1;  // clamped: every address stays in range
+    float part[kRouteQB][8];
+#pragma unroll
+    for (int j = 0; j < kRouteQB; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[j][e] = 0.f;
+    if (p.force == 0) {
+      const uint4* row = reinterpret_cast<const uint4*>(kc_bh + (int64_t)kbc * D);
+#pragma unroll 4
+      for (int i = 0; i < D / 8; ++i) {
+        const uint4 raw = __ldg(row + i);
+        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(k2[e]);
+          kf[2 * e] = f.x;
+          kf[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int j = 0; j < kRouteQB; ++j)
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            part[j][e] = __fadd_rn(part[j][e], __fmul_rn(sq[j][8 * i + e], kf[e]));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kRouteQB; ++j) {
+      if (j >= nq) break;
+      const int qb = qb_lo + j;
+      const float dot = __fadd_rn(__fadd_rn(__fadd_rn(part[j][0], part[j][1]),
+                                            __fadd_rn(part[j][2], part[j][3])),
+                                  __fadd_rn(__fadd_rn(part[j][4], part[j][5]),
+                                            __fadd_rn(part[j][6], part[j][7])));
+      bool sel = false;
+      if (kb < p.nkb) sel = route_rules(p, p.force == 0 && __fmul_rn(dot, p.scale) > scut[j], b, qb, kb);
+      const uint32_t bal = __ballot_sync(0xffffffffu, sel);
+      if (lane == 0) p.masks[((int64_t)bh * p.nqb + qb) * nwords + w] = bal;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_route(const AttnParams& p, int D, cudaStream_t stream) {
+  dim3 grid((p.nqb + kRouteQB - 1) / kRouteQB, p.B * p.H);
+  if (D == 128)
+    route_kernel<128><<<grid, kRouteThreads, 0, stream>>>(p);
+  else
+    route_kernel<64><<<grid, kRouteThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace solattn

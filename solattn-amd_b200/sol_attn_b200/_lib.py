@@ -20,7 +20,7 @@ _P = c_void_p
 SIGNATURES = {
     "solattn_version": (ctypes.c_char_p, []),
     "solattn_strerror": (ctypes.c_char_p, [c_int]),
-    "solattn_workspace_layout": (_I64, [_I64] * 5 + [POINTER(_I64)] * 7),
+    "solattn_workspace_layout": (_I64, [_I64] * 5 + [POINTER(_I64)] * 8),
     "solattn_pool_qkv": (c_int, [_P, _P, _P] + [_I64] * 5 + [_I64] * 9 + [_P, _P, _I64, c_int]
                          + [_P, _P, _P, _P, _P]),
     "solattn_threshold": (c_int, [_P, _P] + [_I64] * 5 + [c_float, c_float] + [_P] * 3 + [_P]),
@@ -70,7 +70,7 @@ def check(rc: int, what: str) -> None:
 
 def workspace_layout(B, Tq, Tk, H, D):
     """Byte offsets and total size of the scratch of one forward call."""
-    offs = [c_int64(0) for _ in range(7)]
+    offs = [c_int64(0) for _ in range(8)]
     total = load().solattn_workspace_layout(B, Tq, Tk, H, D, *[ctypes.byref(o) for o in offs])
-    names = ("kc", "vc", "qc", "mean", "var", "cutoff", "status")
+    names = ("kc", "vc", "qc", "mean", "var", "cutoff", "status", "masks")
     return total, {n: o.value for n, o in zip(names, offs)}

@@ -19,7 +19,7 @@ BLOCK = 64
 
 class Stages:
     def __init__(self, q, k, v, *, beta, scale=None, local=1, kv_sink_blocks=0, q_sink_blocks=0,
-                 protect=None, rows=None, keys=None, debug_mask=False, counts=True):
+                 protect=None, rows=None, keys=None, counts=True):
         self.L = _lib.load()
         self.indexed = rows is not None
         if self.indexed:
@@ -47,8 +47,9 @@ class Stages:
         self.status = torch.zeros(4, dtype=torch.int32, device=dev)
         self.out = torch.empty((B, Tq, H, D), dtype=bf16, device=dev)
         self.counts = torch.full((B, self.nqb, H), -1, dtype=torch.int32, device=dev) if counts else None
-        self.mask = (torch.zeros((B, H, self.nqb, (self.nkb + 31) // 32), dtype=torch.int32, device=dev)
-                     if debug_mask else None)
+        # Routing decisions [B, H, nqb, ceil(nkb/32)] (bit kb % 32 of word kb / 32), written by
+        # the attention call's routing pass.
+        self.mask = torch.zeros((B, H, self.nqb, (self.nkb + 31) // 32), dtype=torch.int32, device=dev)
 
     def _strides(self, x):
         return (0, x.stride(0), x.stride(1)) if self.indexed else (x.stride(0), x.stride(1), x.stride(2))
@@ -87,7 +88,7 @@ class Stages:
             self.protect.data_ptr() if self.protect is not None else None, self.scale,
             self.force, self.local, self.kvs, self.qs, self.out.data_ptr(),
             self.counts.data_ptr() if self.counts is not None else None, self.status.data_ptr(),
-            self.mask.data_ptr() if self.mask is not None else None, stream)
+            self.mask.data_ptr(), stream)
         _lib.check(rc, "solattn_attention")
 
     def run(self, stream=None):

@@ -54,14 +54,13 @@ def to_device(x: torch.Tensor, device="cuda") -> torch.Tensor:
 
 
 class CAbi:
-    """Direct stage-by-stage calls of the C ABI (include/solattn.h) with a debug routing mask."""
+    """Direct stage-by-stage calls of the C ABI (include/solattn.h), routing masks included."""
 
     def stages(self, q, k, v, *, beta, scale=None, local=1, kv_sink_blocks=0, q_sink_blocks=0,
                protect=None, rows=None, keys=None):
         from sol_attn_b200.stages import Stages
         st = Stages(q, k, v, beta=beta, scale=scale, local=local, kv_sink_blocks=kv_sink_blocks,
-                    q_sink_blocks=q_sink_blocks, protect=protect, rows=rows, keys=keys,
-                    debug_mask=True)
+                    q_sink_blocks=q_sink_blocks, protect=protect, rows=rows, keys=keys)
         st.run()
         torch.cuda.synchronize()
         assert int(st.status[0]) == 0, f"device status {int(st.status[0])}"

@@ -44,7 +44,8 @@ def test_workspace_layout():
     assert all(v % 256 == 0 for v in offs.values())
     assert offs["vc"] - offs["kc"] >= 24 * nkb * 128 * 2
     assert offs["mean"] - offs["qc"] >= 24 * nqb * 128 * 4
-    assert total >= offs["cutoff"] + 24 * nqb * 4
+    assert offs["masks"] >= offs["cutoff"] + 24 * nqb * 4
+    assert total >= offs["masks"] + 24 * nqb * (nkb // 32) * 4
     assert _lib.workspace_layout(1, 100, 100, 2, 96)[0] == 0      # unsupported head dim
     assert _lib.workspace_layout(0, 100, 100, 2, 64)[0] == 0      # empty batch
 
