@@ -19,7 +19,7 @@ constexpr int kRouteThreads = 256;
 
 template <int D>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const AttnParams p) {
-  __shared__ float sq[kRouteQB][D];
+  __shared__ __align__(16) float sq[kRouteQB][D];
   __shared__ float scut[kRouteQB];
   const int bh = blockIdx.y;
   const int b = bh / p.H;
@@ -62,10 +62,14 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const AttnParams p
           kf[2 * e + 1] = f.y;
         }
 #pragma unroll
-        for (int j = 0; j < kRouteQB; ++j)
+        for (int j = 0; j < kRouteQB; ++j) {
+          // The q-block means of dims 8i..8i+7: two 16-byte broadcast reads.
+          const float4 qa = *reinterpret_cast<const float4*>(&sq[j][8 * i]);
+          const float4 qb4 = *reinterpret_cast<const float4*>(&sq[j][8 * i + 4]);
+          const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb4.x, qb4.y, qb4.z, qb4.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            part[j][e] = __fadd_rn(part[j][e], __fmul_rn(sq[j][8 * i + e], kf[e]));
+          for (int e = 0; e < 8; ++e) part[j][e] = __fadd_rn(part[j][e], __fmul_rn(qv[e], kf[e]));
+        }
       }
     }
 #pragma unroll

@@ -99,4 +99,9 @@ class Stages:
         return self.out
 
     def launches(self) -> int:
-        return 3 if self.force == 0 else 2
+        """Kernels one run() launches: pool, threshold (threshold mode only), the routing pass
+        (tcgen05 path: BTHD inputs and at most 4096 key blocks) and the fused attention."""
+        n = 2 + (self.force == 0)
+        if not self.indexed and self.nkb <= 4096:
+            n += 1
+        return n
