@@ -163,11 +163,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + L::kMask);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Query tiles of one head are adjacent in launch order so that the CTAs resident at any time
-  // share that head's K/V (16 MB at T=32k) in L2.
-  const int bh = blockIdx.y;
+  // Launch order (one-dimensional grid): first the q-block pairs that hold query-sink blocks
+  // (every key block exact: the longest CTAs) of all heads, so that none of them starts last;
+  // then each head's remaining pairs, head by head, so that the CTAs resident at any time share
+  // that head's K/V (16 MB at T=32k) in L2.
+  const int npairs = (p.nqb + 1) / 2;
+  const int sink_pairs = min(npairs, (p.q_sink_blocks + 1) / 2);
+  int bh, pair;
+  if ((int)blockIdx.x < sink_pairs * p.B * p.H) {
+    bh = (int)blockIdx.x / sink_pairs;
+    pair = (int)blockIdx.x % sink_pairs;
+  } else {
+    const int r = (int)blockIdx.x - sink_pairs * p.B * p.H, rest = npairs - sink_pairs;
+    bh = r / rest;
+    pair = sink_pairs + r % rest;
+  }
   const int b = bh / p.H, h = bh % p.H;
-  const int qb0 = 2 * blockIdx.x;
+  const int qb0 = 2 * pair;
   const bool has1 = qb0 + 1 < p.nqb;
   const int nwords = (p.nkb + 31) / 32;
   int16_t* sTiles = reinterpret_cast<int16_t*>(smem + L::tiles_offset(nwords));
@@ -676,8 +688,9 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
   err = cudaFuncSetAttribute(attn_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
   if (err != cudaSuccess) return err;
-  dim3 grid((p.nqb + 1) / 2, p.B * p.H);
-  attn_sm100_kernel<D><<<grid, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
+  const int64_t ctas = (int64_t)((p.nqb + 1) / 2) * p.B * p.H;
+  if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
+  attn_sm100_kernel<D><<<(unsigned)ctas, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
   return cudaGetLastError();
 }
 

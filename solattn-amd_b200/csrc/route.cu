@@ -14,11 +14,11 @@ namespace solattn {
 
 namespace {
 
-constexpr int kRouteQB = 8;
+constexpr int kRouteQB = 4;
 constexpr int kRouteThreads = 256;
 
 template <int D>
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParams p) {
   __shared__ __align__(16) float sq[kRouteQB][D];
   __shared__ float scut[kRouteQB];
   const int bh = blockIdx.y;

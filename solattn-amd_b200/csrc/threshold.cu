@@ -1,27 +1,37 @@
 // Key moments + Eq. 15 thresholds in one launch (replaces kernels.py:30-64, 211-215).
 //
-// One CTA per (b, h), D threads.  Thread d sums kc[b,h,:,d] and its squares over all key
-// blocks in block order (FP32, no FMA), giving mean and population variance
-// var = max(E[x^2] - E[x]^2, 0) with every block weighted equally (kernels.py:40-47).
-// Then each thread takes q-blocks qb = d, d+D, ... and forms
+// One CTA per (b, h) and group of kThrQB q-blocks, D threads.  Thread d sums kc[b,h,:,d] and
+// its squares over all key blocks in block order (FP32, no FMA), giving mean and population
+// variance var = max(E[x^2] - E[x]^2, 0) with every block weighted equally (kernels.py:40-47);
+// every CTA of a head computes the same moments (the first one writes them out).  The group's
+// Q means are staged in shared memory with coalesced loads, then thread j < kThrQB forms
 //   cutoff = (sum_d qc*mean + beta * sqrt(sum_d (qc*qc)*var)) * scale
-// with sequential sums over d (natural-log units; the fused kernel compares the unscaled
-// proxy dot times scale against it).  All operations are explicitly rounded (__f*_rn) so a
-// CPU restatement in FP32 reproduces the bits.
+// for q-block j of the group with sequential sums over d (natural-log units; the fused kernel
+// compares the unscaled proxy dot times scale against it).  All operations are explicitly
+// rounded (__f*_rn) so a CPU restatement in FP32 reproduces the bits.
 #include "common.cuh"
 
 namespace solattn {
 
+namespace {
+
+constexpr int kThrQB = 32;  // q-blocks per CTA
+
 template <int D>
 __global__ void __launch_bounds__(D) threshold_kernel(const __nv_bfloat16* __restrict__ kc,
-                                                      const float* __restrict__ qc, int H,
-                                                      int nqb, int nkb, float scale, float beta,
+                                                      const float* __restrict__ qc, int nqb,
+                                                      int nkb, float scale, float beta,
                                                       float* mean_out, float* var_out,
                                                       float* cutoff) {
   __shared__ float s_mean[D];
   __shared__ float s_var[D];
-  const int bh = blockIdx.x;
+  __shared__ float s_q[kThrQB][D + 1];  // +1: row-wise reads by different threads hit different banks
+  const int bh = blockIdx.y;
+  const int qb0 = blockIdx.x * kThrQB;
+  const int nq = min(kThrQB, nqb - qb0);
   const int d = threadIdx.x;
+  for (int i = d; i < nq * D; i += D)
+    s_q[i / D][i % D] = qc[((int64_t)bh * nqb + qb0) * D + i];
   const __nv_bfloat16* base = kc + (int64_t)bh * nkb * D + d;
   float s1 = 0.f, s2 = 0.f;
   for (int j = 0; j < nkb; ++j) {
@@ -34,30 +44,36 @@ __global__ void __launch_bounds__(D) threshold_kernel(const __nv_bfloat16* __res
   const float var = fmaxf(__fsub_rn(__fdiv_rn(s2, n), __fmul_rn(mean, mean)), 0.f);
   s_mean[d] = mean;
   s_var[d] = var;
-  mean_out[(int64_t)bh * D + d] = mean;
-  var_out[(int64_t)bh * D + d] = var;
+  if (blockIdx.x == 0) {
+    mean_out[(int64_t)bh * D + d] = mean;
+    var_out[(int64_t)bh * D + d] = var;
+  }
   __syncthreads();
-  for (int qb = d; qb < nqb; qb += D) {
-    const float* qrow = qc + ((int64_t)bh * nqb + qb) * D;
+  if (d < nq) {
     float mu = 0.f, sg = 0.f;
     for (int e = 0; e < D; ++e) {
-      const float qv = qrow[e];
+      const float qv = s_q[d][e];
       mu = __fadd_rn(mu, __fmul_rn(qv, s_mean[e]));
       sg = __fadd_rn(sg, __fmul_rn(__fmul_rn(qv, qv), s_var[e]));
     }
-    cutoff[(int64_t)bh * nqb + qb] = __fmul_rn(__fadd_rn(mu, __fmul_rn(beta, __fsqrt_rn(sg))), scale);
+    cutoff[(int64_t)bh * nqb + qb0 + d] =
+        __fmul_rn(__fadd_rn(mu, __fmul_rn(beta, __fsqrt_rn(sg))), scale);
   }
 }
+
+}  // namespace
 
 cudaError_t launch_threshold(const __nv_bfloat16* kc, const float* qc, int BH, int H, int nqb,
                              int nkb, int D, float scale, float beta, float* mean, float* var,
                              float* cutoff, cudaStream_t stream) {
+  (void)H;
+  const dim3 grid((nqb + kThrQB - 1) / kThrQB, BH);
   if (D == 128)
-    threshold_kernel<128><<<BH, 128, 0, stream>>>(kc, qc, H, nqb, nkb, scale, beta, mean, var,
-                                                  cutoff);
+    threshold_kernel<128><<<grid, 128, 0, stream>>>(kc, qc, nqb, nkb, scale, beta, mean, var,
+                                                    cutoff);
   else
-    threshold_kernel<64><<<BH, 64, 0, stream>>>(kc, qc, H, nqb, nkb, scale, beta, mean, var,
-                                                cutoff);
+    threshold_kernel<64><<<grid, 64, 0, stream>>>(kc, qc, nqb, nkb, scale, beta, mean, var,
+                                                  cutoff);
   return cudaGetLastError();
 }
 
