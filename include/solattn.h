@@ -188,6 +188,18 @@ SOLATTN_API int solattn_sol_forward_noalloc(const void* q, const void* k, const 
 SOLATTN_API int64_t solattn_noalloc_scratch_bytes(void);
 
 /*
+ * Strided 2-D copy between host and device memory on `stream` (no counterpart in the reference,
+ * whose API takes device tensors only): `rows` rows of `width_bytes` bytes, consecutive rows
+ * `src_pitch` / `dst_pitch` bytes apart.  direction 0 = host -> device, 1 = device -> host.
+ * A BTHD tensor's slice of heads [h0, h1) is B*T rows of (h1-h0)*D*2 bytes at pitch H*D*2, so
+ * host-resident inputs can be moved head group by head group (sol_attn_b200.host streams the
+ * groups through the GPU with the copies overlapping the compute).  Pinned host memory is needed
+ * for the copy to be asynchronous.
+ */
+SOLATTN_API int solattn_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                                int64_t width_bytes, int64_t rows, int direction, void* stream);
+
+/*
  * Synchronises `stream`, copies the device status word at `status` to the host, clears it
  * and returns it through *value (0 = no device-side error).  Diagnostic use only: it blocks.
  */

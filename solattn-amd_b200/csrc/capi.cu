@@ -279,6 +279,18 @@ int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_
                            SOLATTN_FORCE_ALL, -1, 0, 0, out, nullptr, nullptr, nullptr, stream);
 }
 
+int solattn_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                    int64_t width_bytes, int64_t rows, int direction, void* stream) {
+  if (!dst || !src || width_bytes <= 0 || rows <= 0 || dst_pitch < width_bytes ||
+      src_pitch < width_bytes || (direction != 0 && direction != 1))
+    return SOLATTN_ERR_ARG;
+  const cudaError_t e = cudaMemcpy2DAsync(
+      dst, (size_t)dst_pitch, src, (size_t)src_pitch, (size_t)width_bytes, (size_t)rows,
+      direction == 0 ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost,
+      static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SOLATTN_OK : SOLATTN_ERR_CUDA;
+}
+
 int solattn_read_status(int32_t* status, int32_t* value, void* stream) {
   if (!status || !value) return SOLATTN_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -4,6 +4,9 @@ Drop-in for the public API of zihaomu/SolAttn-AMD (``src/sol_attn_amd/__init__.p
 """
 
 from .attention import SolStats, dense_attention, sol_attention
+from .host import sol_attention_host
 from .indexed import IndexedPlan, sol_attention_indexed
 
-__all__ = ["SolStats", "dense_attention", "sol_attention", "IndexedPlan", "sol_attention_indexed"]
+# The reference's public names (``__init__.py:6``) plus the host-buffer entry point.
+__all__ = ["SolStats", "dense_attention", "sol_attention", "IndexedPlan", "sol_attention_indexed",
+           "sol_attention_host"]
