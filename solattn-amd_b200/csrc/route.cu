@@ -2,8 +2,9 @@
 // reference.py:41-51), written before the fused attention kernel runs so that the attention
 // CTAs start on their tiles at once.
 //
-// One CTA per (b, h) and group of kRouteQB q-blocks, 256 threads.  Lane kb of a warp reads
-// centroid row kb once (16-byte loads) and forms the proxies of all the group's q-blocks from it,
+// One CTA per (b, h) and group of kRouteQB q-blocks, 256 threads.  A warp stages its 32
+// centroid rows in shared memory with coalesced 16-byte loads, then lane kb forms the proxies
+// of all the group's q-blocks from row kb,
 // with exactly the arithmetic of common.cuh:routing_dot (eight partial sums over d = 8i + j,
 // __fmul_rn / __fadd_rn, combined pairwise), so the decisions are bit-identical to the
 // per-CTA routing of the mma.sync kernel.  One ballot per q-block per 32 key blocks gives a
@@ -37,8 +38,13 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
                             : 0.f;
   __syncthreads();
 
+  // Per-warp staging of its 32 centroid rows, 64 dims at a time: rows are 144 bytes apart so
+  // that the lanes' 16-byte reads of 32 different rows take the minimum 4 wavefronts.
+  constexpr int kRowBytes = 144;
+  __shared__ __align__(16) uint8_t stage[kRouteThreads / 32][32 * kRowBytes];
   const __nv_bfloat16* kc_bh = p.kc + (int64_t)bh * p.nkb * D;
   const int lane = threadIdx.x & 31;
+  uint8_t* my_stage = stage[threadIdx.x >> 5];
   // Warp-uniform loop over 32-block words.
   for (int w = threadIdx.x >> 5; w < nwords; w += kRouteThreads / 32) {
     const int kb = 32 * w + lane;
@@ -49,10 +55,22 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
 #pragma unroll
       for (int e = 0; e < 8; ++e) part[j][e] = 0.f;
     if (p.force == 0) {
-      const uint4* row = reinterpret_cast<const uint4*>(kc_bh + (int64_t)kbc * D);
+#pragma unroll 1
+      for (int half = 0; half < D / 64; ++half) {
+        // Coalesced: 8 consecutive lanes read one row's 128 bytes of these 64 dims.
+        __syncwarp();
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int idx = 32 * t + lane, r = idx >> 3, c = idx & 7;
+          const int kr = min(32 * w + r, p.nkb - 1);  // clamped: every address stays in range
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(kc_bh + (int64_t)kr * D + 64 * half) + c);
+          *reinterpret_cast<uint4*>(my_stage + r * kRowBytes + 16 * c) = v;
+        }
+        __syncwarp();
 #pragma unroll 4
-      for (int i = 0; i < D / 8; ++i) {
-        const uint4 raw = __ldg(row + i);
+      for (int ii = 0; ii < 8; ++ii) {
+        const int i = 8 * half + ii;
+        const uint4 raw = *reinterpret_cast<const uint4*>(my_stage + lane * kRowBytes + 16 * ii);
         const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
         float kf[8];
 #pragma unroll
@@ -70,6 +88,7 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
 #pragma unroll
           for (int e = 0; e < 8; ++e) part[j][e] = __fadd_rn(part[j][e], __fmul_rn(qv[e], kf[e]));
         }
+      }
       }
     }
 #pragma unroll
