@@ -344,7 +344,7 @@ bool attn_sm100_supported(const AttnParams& p);
 // BTHD inputs run on the tcgen05/TMA kernel; gathered (indexed) rows and more than 4096 key
 // blocks use this kernel until the tcgen05 kernel gains a gather producer and a chunked tile list.
 cudaError_t launch_attention(const AttnParams& p, int D, cudaStream_t stream) {
-  if (p.q.idx == nullptr && p.k.idx == nullptr && attn_sm100_supported(p))
+  if (attn_sm100_supported(p))
     return launch_attn_sm100(p, D, stream);
   return launch_attn_mma(p, D, stream);
 }

@@ -33,6 +33,8 @@
 //              the V ring (slot refilled when P V has completed).
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 #include "sm100.cuh"
 
 namespace solattn {
@@ -125,6 +127,54 @@ __device__ __forceinline__ void load_kv_tile(uint32_t dst, const CUtensorMap* ti
     tma_load_4d(dst + j * kKVBox, cent ? cent_map : tile_map, full, 64 * j, row, h, b);
 }
 
+// Row indices of a gathered tile, loaded ahead into registers: lane l holds the token index of
+// rows l, l + 32, ... (ROWS / 32 of them), row r taken from idx[min(r, valid - 1)].  An index
+// outside [0, x.rows) is reported (kStatusBadIndex) and replaced by 0, so every address
+// computed from it stays in range.
+template <int ROWS>
+struct RowIdx {
+  int64_t t[ROWS / 32];
+};
+template <int ROWS>
+__device__ __forceinline__ RowIdx<ROWS> load_row_idx(const TensorView& x, const int64_t* idx,
+                                                     int valid, int lane, int32_t* status) {
+  RowIdx<ROWS> ri;
+#pragma unroll
+  for (int k = 0; k < ROWS / 32; ++k) {
+    int64_t tok = __ldg(idx + min(32 * k + lane, valid - 1));
+    if (tok < 0 || tok >= x.rows) {
+      report(status, kStatusBadIndex);
+      tok = 0;
+    }
+    ri.t[k] = tok;
+  }
+  return ri;
+}
+
+// Gathered rows (indexed inputs): the ROWS rows of head h named by `ri`, copied from the NHD
+// tensor x with 16-byte cp.async into a 128-byte-swizzled K-major tile at `dst` (64-column
+// boxes `box_bytes` apart; 16-byte chunk c of row r lands at chunk c ^ (r % 8), the layout a
+// tiled TMA load produces).  D/8 consecutive lanes cover one row, so every warp instruction
+// reads whole rows.  The calling lane then arms `full` for one arrival when its copies have
+// landed.
+template <int D, int ROWS>
+__device__ __forceinline__ void gather_tile(uint32_t dst, uint32_t box_bytes, const TensorView& x,
+                                            const RowIdx<ROWS>& ri, int h, int lane,
+                                            uint32_t full) {
+  constexpr int kChunks = D / 8;              // 16-byte chunks per row
+  constexpr int kRowsPerPass = 32 / kChunks;  // rows one warp instruction covers (2 or 4)
+  const int q = lane % kChunks, j = q >> 3, c = q & 7;
+  const __nv_bfloat16* base = x.ptr + (int64_t)h * x.sH + 8 * q;
+#pragma unroll
+  for (int r0 = 0; r0 < ROWS; r0 += kRowsPerPass) {
+    const int r = r0 + lane / kChunks;
+    const int64_t tok = __shfl_sync(0xffffffffu, ri.t[r0 / 32], r & 31);
+    cp_async16(dst + (uint32_t)j * box_bytes + (uint32_t)(r * 128 + ((c ^ (r & 7)) * 16)),
+               base + tok * x.sT, 16);
+  }
+  cp_async_mbar_arrive_noinc(full);
+}
+
 // Row max of 64 scores with three-input max instructions: eight independent chains.
 __device__ __forceinline__ float row_max64(const uint32_t (&s)[2][32]) {
   float m[8];
@@ -187,6 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < NBARS; ++i) {
       uint32_t count = 1;
+      // Gathered loads arrive once per producer lane (cp.async completions).
+      if (i == Q_FULL && p.q.idx) count = 32;
+      if (((i >= K_FULL && i < K_FULL + kStages) || (i >= V_FULL && i < V_FULL + kStages)) && p.k.idx)
+        count = 32;
       if (i >= P_FULL && i < P_FULL + kStages) count = kGroupWarps;
       if (i >= MERGE && i < MERGE + 4) count = 2;
       mbar_init(bar(i), count);
@@ -219,15 +273,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (tid == kKWarp * 32) {  // Q starts loading at once
-    tma_prefetch(&tmQ);
-    tma_prefetch(&tmK);
-    tma_prefetch(&tmV);
-    tma_prefetch(&tmKC);
-    tma_prefetch(&tmVC);
-    mbar_expect_tx(bar(Q_FULL), L::kQTile);
-    for (int j = 0; j < D / 64; ++j)
-      tma_load_4d(sQ + j * kQBox, &tmQ, bar(Q_FULL), 64 * j, qb0 * kBlock, h, b);
+  if (warp == kKWarp) {  // Q starts loading at once
+    if (p.q.idx) {
+      const RowIdx<kRows> ri = load_row_idx<kRows>(
+          p.q, p.q.idx + (int64_t)b * p.Tq + (int64_t)qb0 * kBlock, p.Tq - qb0 * kBlock, lane,
+          p.status);
+      gather_tile<D, kRows>(sQ, kQBox, p.q, ri, h, lane, bar(Q_FULL));
+    } else if (lane == 0) {
+      tma_prefetch(&tmQ);
+      mbar_expect_tx(bar(Q_FULL), L::kQTile);
+      for (int j = 0; j < D / 64; ++j)
+        tma_load_4d(sQ + j * kQBox, &tmQ, bar(Q_FULL), 64 * j, qb0 * kBlock, h, b);
+    }
+    if (lane == 0) {
+      if (!p.k.idx) {
+        tma_prefetch(&tmK);
+        tma_prefetch(&tmV);
+      }
+      tma_prefetch(&tmKC);
+      tma_prefetch(&tmVC);
+    }
   }
 
   // ---- tile list (warp 0) and exact-block counts ----
@@ -280,30 +345,66 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ntiles = (int)misc[2];
 
   if (warp == kKWarp) {
-    // ------------------------------------------------------------------ TMA producer: K, V rings
+    // ------------------------------------------------------------------ producer: K, V rings
     // Slot s of the K ring is free once S_{i - kStages} has completed, slot s of the V ring once
     // P_{i - kStages} V_{i - kStages} has; S_i itself waits for the latter, so loading K_i
-    // before that wait delays nothing.
-    if (lane == 0) {
-      int k_issued = 0, v_issued = 0;
+    // before that wait delays nothing.  Without gathers lane 0 alone runs the loop and issues
+    // TMA loads; gathered rows are copied by the whole warp.
+    int k_issued = 0, v_issued = 0;
+    if (!p.k.idx) {
+      if (lane == 0) {
+        for (int i = 0; i < ntiles; ++i) {
+          const int s = i % kStages;
+          const uint32_t prev = (uint32_t)(i / kStages - 1) & 1u;  // parity of the last use
+          if (i >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) break;
+          load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), sTiles[i], h, b);
+          ++k_issued;
+          if (i >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) break;
+          load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), sTiles[i], h, b);
+          ++v_issued;
+        }
+      }
+    } else {
+      // Gathered K/V rows: the whole warp copies; a tile's 64 row indices (shared by K and V)
+      // are loaded one tile ahead.  Centroid tiles still come by TMA (lane 0), the other lanes
+      // arriving on the barrier, which counts one arrival per lane in this mode.
+      const int64_t* kvidx = p.k.idx + (int64_t)b * p.Tk;
+      auto row_idx = [&](int e) {
+        RowIdx<kKeys> ri;
+        if (e >= 0) {
+          ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, p.Tk - e * kBlock, lane,
+                                   p.status);
+        } else {
+          ri.t[0] = ri.t[1] = 0;
+        }
+        return ri;
+      };
+      RowIdx<kKeys> ri = row_idx(ntiles > 0 ? sTiles[0] : -1);
       for (int i = 0; i < ntiles; ++i) {
         const int s = i % kStages;
-        const uint32_t prev = (uint32_t)(i / kStages - 1) & 1u;  // parity of the slot's last use
-        if (i >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) break;
-        load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), sTiles[i], h, b);
+        const uint32_t prev = (uint32_t)(i / kStages - 1) & 1u;
+        const int e = sTiles[i];
+        if (i >= kStages && !warp_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) break;
+        if (e >= 0) gather_tile<D, kKeys>(sK + s * L::kKVTile, kKVBox, p.k, ri, h, lane, bar(K_FULL + s));
+        else if (lane == 0) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, h, b);
+        else mbar_arrive(bar(K_FULL + s));
         ++k_issued;
-        if (i >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) break;
-        load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), sTiles[i], h, b);
+        if (i >= kStages && !warp_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) break;
+        if (e >= 0) gather_tile<D, kKeys>(sV + s * L::kKVTile, kKVBox, p.v, ri, h, lane, bar(V_FULL + s));
+        else if (lane == 0) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, h, b);
+        else mbar_arrive(bar(V_FULL + s));
         ++v_issued;
+        if (i + 1 < ntiles) ri = row_idx(sTiles[i + 1]);
       }
-      if (*abort_flag) {  // never leave while a bulk copy may still write shared memory
-        mbar_wait_quiet(bar(Q_FULL), 0);
-        for (int s = 0; s < kStages; ++s) {
-          int n = loads_into(k_issued, s);
-          if (n) mbar_wait_quiet(bar(K_FULL + s), (uint32_t)(n - 1) & 1u);
-          n = loads_into(v_issued, s);
-          if (n) mbar_wait_quiet(bar(V_FULL + s), (uint32_t)(n - 1) & 1u);
-        }
+      cp_async_wait_all();  // never leave while a copy may still write shared memory
+    }
+    if (lane == 0 && *abort_flag) {
+      mbar_wait_quiet(bar(Q_FULL), 0);
+      for (int s = 0; s < kStages; ++s) {
+        int n = loads_into(k_issued, s);
+        if (n) mbar_wait_quiet(bar(K_FULL + s), (uint32_t)(n - 1) & 1u);
+        n = loads_into(v_issued, s);
+        if (n) mbar_wait_quiet(bar(V_FULL + s), (uint32_t)(n - 1) & 1u);
       }
     }
     __syncwarp();
@@ -319,6 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           !warp_wait(bar(V_FULL + s), ph, abort_flag, p.status))
         break;
       tc_fence_after();
+      if (p.k.idx) fence_proxy_async_smem();  // gathered V rows were written by cp.async
       if (lane == 0) {
         const uint64_t vd = dV + (uint64_t)s * kSlotStep;
         const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
@@ -344,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t dQ = smem_desc_sw128(sQ, 16, 1024);
     const uint64_t dK = smem_desc_sw128(sK, 16, 1024);
     if (warp_wait(bar(Q_FULL), 0, abort_flag, p.status)) {
+      if (p.q.idx) fence_proxy_async_smem();  // gathered Q rows were written by cp.async
       for (int i = par; i < ntiles; i += 2) {
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)(i / kStages) & 1u;
@@ -354,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i >= kStages && !warp_wait(bar(PV_DONE + s), ph ^ 1u, abort_flag, p.status)) break;
         if (!warp_wait(bar(K_FULL + s), ph, abort_flag, p.status)) break;
         tc_fence_after();
+        if (p.k.idx) fence_proxy_async_smem();  // gathered K rows were written by cp.async
         if (lane == 0) {
           const uint64_t kd = dK + (uint64_t)s * kSlotStep;
           const uint32_t tS = tmem + kTmemS + (uint32_t)(kKeys * s);
@@ -672,10 +776,14 @@ bool make_pooled_map(CUtensorMap* map, const __nv_bfloat16* base, int B, int H, 
 template <int D>
 cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
   if (p.nkb > kMaxKeyBlocks || (p.masks == nullptr && p.force == 0)) return cudaErrorInvalidValue;
+  // Gathered (indexed) inputs are copied by the producer warp and need no tensor map.
   CUtensorMap tmQ, tmK, tmV, tmKC, tmVC;
-  if (!make_bthd_map(&tmQ, p.q, p.B, p.Tq, p.H, D, kRows) ||
-      !make_bthd_map(&tmK, p.k, p.B, p.Tk, p.H, D, kBlock) ||
-      !make_bthd_map(&tmV, p.v, p.B, p.Tk, p.H, D, kBlock) ||
+  memset(&tmQ, 0, sizeof(tmQ));
+  memset(&tmK, 0, sizeof(tmK));
+  memset(&tmV, 0, sizeof(tmV));
+  if ((!p.q.idx && !make_bthd_map(&tmQ, p.q, p.B, p.Tq, p.H, D, kRows)) ||
+      (!p.k.idx && (!make_bthd_map(&tmK, p.k, p.B, p.Tk, p.H, D, kBlock) ||
+                    !make_bthd_map(&tmV, p.v, p.B, p.Tk, p.H, D, kBlock))) ||
       !make_pooled_map(&tmKC, p.kc, p.B, p.H, p.nkb, D) ||
       !make_pooled_map(&tmVC, p.vc, p.B, p.H, p.nkb, D))
     return cudaErrorInvalidValue;
