@@ -62,7 +62,8 @@ SOLATTN_API const char* solattn_strerror(int code);
  * Scratch layout of one forward call.  Replaces the torch.empty allocations of the
  * reference launcher (kernels.py:185-190, 203-217): kc/vc (BF16 K/V block means), qc (FP32
  * Q block means), mean/var (FP32 key moments), cutoff (FP32 Eq. 15 thresholds), one device
- * status word, and masks (the routing decisions, uint32 bitmask [B, H, nqb, ceil(nkb/32)]).
+ * status word, and masks (the routing decisions, uint32 bitmask [B, H, nqb, ceil(nkb/32)],
+ * followed by one uint32 work counter).
  * Offsets are in bytes from the workspace base, each 256-byte aligned.  The pooled tensors
  * use the layout [B, H, blocks, D]; cutoff is [B, H, nqb].
  * Returns the total size in bytes, or 0 on an invalid shape.
@@ -115,8 +116,11 @@ SOLATTN_API int solattn_threshold(const void* kc, const float* qc, int64_t B, in
  * force != 0.  counts may be NULL.  status may be NULL.
  * masks receives the routing decisions as a bitmask [B, H, nqb, ceil(nkb/32)] of uint32
  * words (bit kb%32 of word kb/32 set = block kb exact); the call writes it in a routing pass
- * and the attention kernel reads it back.  It is required when force == SOLATTN_FORCE_THRESHOLD
- * and may be NULL in the force modes (the rules are then evaluated inside the kernel).
+ * and the attention kernel reads it back.  The buffer holds B*H*nqb*ceil(nkb/32) + 1 words:
+ * the last one is the attention kernel's work counter (zeroed by the routing pass, then
+ * incremented as the persistent CTAs take work items).  It is required when
+ * force == SOLATTN_FORCE_THRESHOLD and may be NULL in the force modes (the rules are then
+ * evaluated inside the kernel and the work is split round robin).
  */
 SOLATTN_API int solattn_attention(const void* q, const void* k, const void* v,
                       int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,

@@ -1,36 +1,45 @@
 // Fused routed attention on the Blackwell data path (replaces `_sol`, kernels.py:101-182).
 //
-// One CTA per SM (it allocates all 512 TMEM columns) = one 128-row query tile = two 64-row
-// q-blocks (qb0 = 2*x, qb0 + 1) of one (b, h); 384 threads.
+// Persistent kernel: one CTA per SM (it allocates all 512 TMEM columns) works through a list of
+// work items, item k of CTA c being item c + k * gridDim.x of the launch order.  An item is one
+// 128-row query tile = two 64-row q-blocks (qb0, qb0 + 1) of one (b, h).  Launch order: first
+// the q-block pairs holding query-sink blocks of all heads (every key block exact: the longest
+// items), then each head's remaining pairs head by head (the items in flight at one time share
+// one head's K/V in L2).  384 threads.
 //
 // Tiles hold 64 keys: one exact key block, or 64 pooled centroids.  The routing pass
-// (route.cu) has already written every q-block's exact-block bitmask; the tile list (shared
-// memory, built by warp 0) holds first every 64-centroid group that still has a block
-// unselected by either q-block (entry -(t + 1)), then every block of the union of both
-// q-blocks' exact sets in increasing order (entry kb >= 0).  A row whose q-block did not select
-// an exact block sees it as -inf; a centroid whose block is exact for the row's q-block too.
+// (route.cu) has already written every q-block's exact-block bitmask; an item's tile list
+// (shared memory) holds first every 64-centroid group that still has a block unselected by
+// either q-block (entry -(t + 1)), then every block of the union of both q-blocks' exact sets
+// in increasing order (entry kb >= 0).  A row whose q-block did not select an exact block sees
+// it as -inf; a centroid whose block is exact for the row's q-block too.
 //
-// Two independent online softmaxes run side by side: group g (softmax warps 4g..4g+3) takes
-// the tiles i with i % 2 == g into its own accumulator O_g with its own running max and sum;
-// the epilogue merges the two.  The two warps that share an SM sub-partition therefore work on
-// different tiles and overlap, instead of waiting on each other.
+// The tiles of all of a CTA's items form one sequence: tile g (counted over the CTA's items)
+// uses ring slot / S buffer g % kStages and softmax group g % 2, so the rings and the tensor
+// core run on from one item into the next.  Two independent online softmaxes run side by side:
+// group x (softmax warps 4x..4x+3) takes the tiles with g % 2 == x into its own accumulator O_x
+// with its own running max and sum; the item's epilogue merges the two.
 //
 // TMEM (512 columns): O_0 at [0, 128), O_1 at [128, 256), and kStages S buffers of 64 columns
 // at [256, 512); P (BF16 pairs) is written over the first 32 columns of its S buffer.
-// Shared memory: Q (TMA, read by every S MMA), K and V rings of kStages 64-row tiles each.
+// Shared memory: two Q buffers (items alternate), K and V rings of kStages 64-row tiles, and two
+// sets of routing bitmasks and tile lists (items alternate).
 //
-// Warp roles (tile i uses ring slot / S buffer i % kStages):
+// Warp roles:
 //   warps 0-7  softmax: warp w owns TMEM lanes 32(w%4)..+31 for the tiles of group w/4.  Per
 //              tile: tcgen05.ld S, mask/bias, FP32 online softmax with lazy rescaling, P
 //              written over the S buffer, arrive P_FULL.  A warp whose q-block does not use
-//              the tile writes P = 0 without reading S.  Epilogue: merge O_0 and O_1 -> BF16.
+//              the tile writes P = 0 without reading S.  Item epilogue: merge O_0 and O_1 ->
+//              BF16, then O_FREE (the next item's P V may overwrite O).
 //   warps 8-9  S issue for even / odd tiles (lane 0 issues; the whole warp runs the loop so
-//              that addresses stay warp-uniform): S_i = Q K_i^T once P_{i-kStages} V has freed
-//              the buffer and K_i has landed.  One thread issues a dependent tcgen05.mma about
+//              that addresses stay warp-uniform): S_g = Q K_g^T once P_{g-kStages} V has freed
+//              the buffer and K_g has landed.  One thread issues a dependent tcgen05.mma about
 //              every 100 cycles; two issuers keep the 8 MMAs (N = 64) per tile flowing.
-//   warp 10    P V issue: O_{i%2} += P_i V_i once the group's four warps have written P_i.
-//   warp 11    TMA producer: Q once, then the K ring (slot refilled when S has completed) and
-//              the V ring (slot refilled when P V has completed).
+//   warp 10    P V issue: O_{g%2} += P_g V_g once the group's four warps have written P_g.
+//   warp 11    producer: per item, the routing bitmasks, the tile list and the exact-block
+//              counts (built one item ahead), Q; then the K ring (slot refilled when S has
+//              completed) and the V ring (slot refilled when P V has completed), by TMA, or by
+//              gathering rows with cp.async for indexed inputs.
 #include <cudaTypedefs.h>
 
 #include <cstring>
@@ -43,23 +52,28 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kRows = 128;         // query rows per CTA
+constexpr int kRows = 128;         // query rows per item
 constexpr int kKeys = 64;          // keys per tile
 constexpr int kStages = 4;         // S buffers = K slots = V slots
 constexpr int kGroupWarps = 4;     // softmax warps per group (one per TMEM lane quarter)
+constexpr int kSoftmaxWarps = 8;
 constexpr int kSWarp0 = 8;         // S issue, even tiles (kSWarp0 + 1: odd tiles)
 constexpr int kPVWarp = 10;        // P V issue
-constexpr int kKWarp = 11;         // TMA producer: Q and the K and V rings
+constexpr int kKWarp = 11;         // producer
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 0, kTmemS = 256;  // O_g at kTmemO + 128 g
+constexpr uint32_t kTmemO = 0, kTmemS = 256;  // O_x at kTmemO + 128 x
 constexpr int kQBox = kRows * 128;   // one 128-row x 64-column BF16 box of Q (16 KB)
 constexpr int kKVBox = kKeys * 128;  // one 64-row x 64-column BF16 box of K or V (8 KB)
 constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
+// Readers of an item's tile list that must be done before the producer overwrites it two items
+// later: the softmax warps, the two S issuers and the P V issuer.
+constexpr int kListReaders = kSoftmaxWarps + 3;
 
-// Barriers; ring barriers are indexed by slot.
+// Barriers; ring barriers are indexed by slot, item barriers by item parity.
 enum Bar {
-  Q_FULL,
+  Q_FULL, Q_EMPTY = Q_FULL + 2, LIST_FULL = Q_EMPTY + 2, LIST_EMPTY = LIST_FULL + 2,
+  O_FREE = LIST_EMPTY + 2,
   K_FULL, K_EMPTY = K_FULL + kStages, V_FULL = K_EMPTY + kStages, S_FULL = V_FULL + kStages,
   P_FULL = S_FULL + kStages, PV_DONE = P_FULL + kStages,
   MERGE = PV_DONE + kStages,  // [4 lane quarters], two arrivals each: the epilogue exchange
@@ -70,18 +84,19 @@ template <int D>
 struct Layout {
   static constexpr int kQTile = kRows * D * 2;   // 128 x D BF16
   static constexpr int kKVTile = kKeys * D * 2;  // 64 x D BF16
-  static constexpr int kQ = 0;
-  static constexpr int kK = kQTile;
+  static constexpr int kQ = 0;                   // two Q buffers
+  static constexpr int kK = 2 * kQTile;
   static constexpr int kV = kK + kStages * kKVTile;
   static constexpr int kBars = kV + kStages * kKVTile;
-  static constexpr int kMisc = kBars + NBARS * 8;   // [0] TMEM address [1] abort [2] tiles
-  static constexpr int kMerge = kMisc + 16;         // float [8 warps][2][32 lanes]: m, l
-  static constexpr int kMask = kMerge + 8 * 2 * 32 * 4;  // uint32 [2][nwords]
-  __host__ __device__ static int tiles_offset(int nwords) { return kMask + 2 * nwords * 4; }  // int16
+  // uint32 [0] TMEM address [1] abort flag [2 + j] tiles, [4 + j] item of list buffer j
+  static constexpr int kMisc = kBars + NBARS * 8;
+  static constexpr int kMerge = kMisc + 32;  // float [2 items][8 warps][2][32 lanes]: m, l
+  static constexpr int kMask = kMerge + 2 * 8 * 2 * 32 * 4;  // uint32 [2 items][2 q-blocks][nwords]
+  __host__ __device__ static int tiles_offset(int nwords) { return kMask + 4 * nwords * 4; }
   __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + nkb; }
-  static size_t bytes(int nkb) {
+  static size_t bytes(int nkb) {  // int16 tile lists [2 items][max_tiles]
     const int nwords = (nkb + 31) / 32;
-    return 1024 + (size_t)tiles_offset(nwords) + (size_t)max_tiles(nkb) * 2;
+    return 1024 + (size_t)tiles_offset(nwords) + 2 * (size_t)max_tiles(nkb) * 2;
   }
 };
 
@@ -190,6 +205,207 @@ __device__ __forceinline__ float row_max64(const uint32_t (&s)[2][32]) {
   return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
+
+// Position of work item `item` in the launch order: the q-block pairs holding query-sink blocks
+// of every head first (the longest items: every key block exact), then each head's remaining
+// pairs, head by head.
+struct ItemPos {
+  int b, h, bh, qb0;
+};
+__device__ __forceinline__ ItemPos item_pos(int item, int nqb, int q_sink_blocks, int B, int H) {
+  const int npairs = (nqb + 1) / 2;
+  const int sink_pairs = min(npairs, (q_sink_blocks + 1) / 2);
+  int bh, pair;
+  if (item < sink_pairs * B * H) {
+    bh = item / sink_pairs;
+    pair = item % sink_pairs;
+  } else {
+    const int r = item - sink_pairs * B * H, rest = npairs - sink_pairs;
+    bh = r / rest;
+    pair = sink_pairs + r % rest;
+  }
+  ItemPos ip;
+  ip.bh = bh;
+  ip.b = bh / H;
+  ip.h = bh % H;
+  ip.qb0 = 2 * pair;
+  return ip;
+}
+__device__ __forceinline__ ItemPos item_pos(const AttnParams& p, int item) {
+  return item_pos(item, p.nqb, p.q_sink_blocks, p.B, p.H);
+}
+
+// An item's routing mask words (both q-blocks, 2 nwords <= 256 words), loaded into registers one
+// item ahead so that the load latency is off the producer's path: lane l holds word l + 32 j.
+constexpr int kMaskRegs = 2 * (kMaxKeyBlocks / 32) / 32;
+struct MaskWords {
+  uint32_t w[kMaskRegs];
+};
+__device__ __forceinline__ MaskWords load_mask_words(const AttnParams& p, int item, int total,
+                                                     int nwords, int lane) {
+  MaskWords mw;
+#pragma unroll
+  for (int j = 0; j < kMaskRegs; ++j) mw.w[j] = 0u;
+  if (!p.masks || item >= total) return mw;
+  const ItemPos ip = item_pos(p, item);
+#pragma unroll
+  for (int j = 0; j < kMaskRegs; ++j) {
+    const int i = 32 * j + lane;
+    if (i < 2 * nwords) {
+      const int qb = ip.qb0 + i / nwords;
+      if (qb < p.nqb) mw.w[j] = __ldg(p.masks + ((int64_t)ip.bh * p.nqb + qb) * nwords + (i % nwords));
+    }
+  }
+  return mw;
+}
+
+// One warp: both q-blocks' exact-block bitmasks of an item into m[0, 2 nwords) -- the routing
+// pass's words (loaded ahead into `mw`), or (force modes without a mask buffer) the force /
+// local / sink / protected rules alone -- then the item's tile list into `tiles`: the useful
+// 64-centroid groups, then the union of both exact sets in increasing order.  Writes the
+// per-q-block exact counts when requested and returns the number of tiles (warp-uniform).
+__device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPos& ip,
+                                               const MaskWords& mw, uint32_t* m, int16_t* tiles,
+                                               int nwords, int lane) {
+  const bool has1 = ip.qb0 + 1 < p.nqb;
+  if (p.masks) {
+#pragma unroll
+    for (int j = 0; j < kMaskRegs; ++j)
+      if (32 * j + lane < 2 * nwords) m[32 * j + lane] = mw.w[j];
+  } else {
+    for (int i = 0; i < 2 * nwords; ++i) {
+      const int qb = ip.qb0 + i / nwords, kb = 32 * (i % nwords) + lane;
+      const bool sel = qb < p.nqb && kb < p.nkb && route_rules(p, false, ip.b, qb, kb);
+      const uint32_t bal = __ballot_sync(0xffffffffu, sel);
+      if (lane == 0) m[i] = bal;
+    }
+  }
+  __syncwarp();
+  const uint32_t* m0 = m;
+  const uint32_t* m1 = m + nwords;
+  int n = 0;
+  const int nct = p.force == 1 ? 0 : (p.nkb + kKeys - 1) / kKeys;
+  for (int t0 = 0; t0 < nct; t0 += 32) {
+    const int t = t0 + lane;
+    bool useful = false;
+    if (t < nct) {
+      for (int wi = 2 * t; wi < 2 * t + 2 && wi < nwords; ++wi) {
+        const uint32_t v = valid_word(wi, p.nkb);
+        if ((~m0[wi] & v) || (has1 && (~m1[wi] & v))) useful = true;
+      }
+    }
+    const uint32_t bal = __ballot_sync(0xffffffffu, useful);
+    if (useful) tiles[n + __popc(bal & ((1u << lane) - 1u))] = (int16_t)(-(t + 1));
+    n += __popc(bal);
+  }
+  int r = 0;
+  for (int w0 = 0; w0 < nwords; w0 += 32) {
+    const int wi = w0 + lane;
+    uint32_t bits = 0u;
+    if (wi < nwords) bits = m0[wi] | (has1 ? m1[wi] : 0u);
+    const int cnt = __popc(bits);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int rank = n + r + incl - cnt;
+    while (bits) {
+      const int bit = __ffs(bits) - 1;
+      bits &= bits - 1u;
+      tiles[rank++] = (int16_t)(32 * wi + bit);
+    }
+    r += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane < 2 && p.counts && ip.qb0 + lane < p.nqb) {
+    int c = 0;
+    for (int i = 0; i < nwords; ++i) c += __popc(m[lane * nwords + i]);
+    p.counts[((int64_t)ip.b * p.nqb + ip.qb0 + lane) * p.H + ip.h] = c;
+  }
+  __syncwarp();
+  return n + r;
+}
+
+// Item epilogue of one softmax warp: wait for the group's last P V, exchange the running max
+// and sum with the partner warp (same TMEM lanes, other group; the exchange buffer alternates
+// with the items, so a warp that has run ahead never overwrites values not yet read), merge O_0
+// and O_1 for the warp's 32 rows and half of the head dims into BF16, releasing both
+// accumulators (the next item's P V may start) as soon as they are read, then the item's tile
+// list.  Returns false after an abort.
+template <int D>
+__device__ __forceinline__ bool item_epilogue(uint32_t tmem, uint32_t bar0, int warp, int lane, int k,
+                                           int last, float m_run, float l_run, int ntiles, int g,
+                                           int item, float* sMerge, volatile int* abort_flag,
+                                           int32_t* status, __nv_bfloat16* out, int Tq, int H,
+                                           int nqb, int q_sink_blocks, int B) {
+  auto bar = [bar0](int i) { return bar0 + 8u * (uint32_t)i; };
+  const int quarter = warp & 3, grp = warp >> 2, lb = k & 1;
+  const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+  if (last >= 0 &&
+      !warp_wait(bar(PV_DONE + last % kStages), (uint32_t)(last / kStages) & 1u, abort_flag, status))
+    return false;
+  const float m_me = last >= 0 ? m_run : -INFINITY;
+  float* mg = sMerge + lb * (8 * 2 * 32);
+  mg[(warp * 2) * 32 + lane] = m_me;
+  mg[(warp * 2 + 1) * 32 + lane] = l_run;
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar(MERGE + quarter));
+  if (!warp_wait(bar(MERGE + quarter), (uint32_t)k & 1u, abort_flag, status)) return false;
+  tc_fence_after();
+  const float m_o = mg[((warp ^ 4) * 2) * 32 + lane];
+  const float l_o = mg[((warp ^ 4) * 2 + 1) * 32 + lane];
+  const float m0 = grp == 0 ? m_me : m_o, m1 = grp == 0 ? m_o : m_me;
+  const float l0 = grp == 0 ? l_run : l_o, l1 = grp == 0 ? l_o : l_run;
+  const float m = fmaxf(m0, m1);
+  const float f0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
+  const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
+  const float inv = 1.f / (l0 * f0 + l1 * f1);
+  // A group without tiles in this item holds another item's accumulator: it is skipped.
+  const bool has0 = ntiles >= 2 || (ntiles == 1 && (g & 1) == 0);
+  const bool has1 = ntiles >= 2 || (ntiles == 1 && (g & 1) == 1);
+  const ItemPos ip = item_pos(item, nqb, q_sink_blocks, B, H);
+  const int grow = ip.qb0 * kBlock + quarter * 32 + lane;
+  // This warp writes head dims [grp * D / 2, (grp + 1) * D / 2) of its 32 rows.
+  __nv_bfloat16* dst = out + (((int64_t)ip.b * Tq + grow) * H + ip.h) * D + grp * (D / 2);
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {  // 16 columns at a time
+    const uint32_t col = (uint32_t)(grp * (D / 2) + 16 * c);
+    uint32_t o0[16], o1[16];
+    if (has0) tmem_ld16(tmem + kTmemO + lane_base + col, o0);
+    if (has1) tmem_ld16(tmem + kTmemO + 128 + lane_base + col, o1);
+    tmem_wait_ld();
+    if (c == D / 32 - 1) {
+      // Both accumulators read: the next item's P V may start.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(O_FREE));
+    }
+    if (grow < Tq) {
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float a0 = 0.f, a1 = 0.f;
+        if (has0) {
+          a0 = __uint_as_float(o0[2 * j]) * f0;
+          a1 = __uint_as_float(o0[2 * j + 1]) * f0;
+        }
+        if (has1) {
+          a0 = fmaf(__uint_as_float(o1[2 * j]), f1, a0);
+          a1 = fmaf(__uint_as_float(o1[2 * j + 1]), f1, a1);
+        }
+        w[j] = pack_bf16(a0 * inv, a1 * inv);
+      }
+      uint4* d4 = reinterpret_cast<uint4*>(dst + 16 * c);
+      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar(LIST_EMPTY + lb));
+  return true;
+}
+
 }  // namespace
 
 
@@ -208,84 +424,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar0 = sbase + L::kBars;
   auto bar = [bar0](int i) { return bar0 + 8u * (uint32_t)i; };
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile uint32_t* vmisc = misc;  // the list words are rewritten while the kernel runs
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   float* sMerge = reinterpret_cast<float*>(smem + L::kMerge);
-  uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + L::kMask);
+  const int nwords = (p.nkb + 31) / 32;
+  const int max_tiles = L::max_tiles(p.nkb);
+  uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + L::kMask);                // [2][2][nwords]
+  int16_t* sTiles = reinterpret_cast<int16_t*>(smem + L::tiles_offset(nwords));  // [2][max_tiles]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Launch order (one-dimensional grid): first the q-block pairs that hold query-sink blocks
-  // (every key block exact: the longest CTAs) of all heads, so that none of them starts last;
-  // then each head's remaining pairs, head by head, so that the CTAs resident at any time share
-  // that head's K/V (16 MB at T=32k) in L2.
-  const int npairs = (p.nqb + 1) / 2;
-  const int sink_pairs = min(npairs, (p.q_sink_blocks + 1) / 2);
-  int bh, pair;
-  if ((int)blockIdx.x < sink_pairs * p.B * p.H) {
-    bh = (int)blockIdx.x / sink_pairs;
-    pair = (int)blockIdx.x % sink_pairs;
-  } else {
-    const int r = (int)blockIdx.x - sink_pairs * p.B * p.H, rest = npairs - sink_pairs;
-    bh = r / rest;
-    pair = sink_pairs + r % rest;
-  }
-  const int b = bh / p.H, h = bh % p.H;
-  const int qb0 = 2 * pair;
-  const bool has1 = qb0 + 1 < p.nqb;
-  const int nwords = (p.nkb + 31) / 32;
-  int16_t* sTiles = reinterpret_cast<int16_t*>(smem + L::tiles_offset(nwords));
+  const int total = ((p.nqb + 1) / 2) * p.B * p.H;  // work items
 
   if (tid == 0) {
     for (int i = 0; i < NBARS; ++i) {
       uint32_t count = 1;
       // Gathered loads arrive once per producer lane (cp.async completions).
-      if (i == Q_FULL && p.q.idx) count = 32;
+      if (i >= Q_FULL && i < Q_FULL + 2 && p.q.idx) count = 32;
       if (((i >= K_FULL && i < K_FULL + kStages) || (i >= V_FULL && i < V_FULL + kStages)) && p.k.idx)
         count = 32;
+      if (i >= Q_EMPTY && i < Q_EMPTY + 2) count = 2;  // both S issuers
+      if (i >= LIST_EMPTY && i < LIST_EMPTY + 2) count = kListReaders;
+      if (i == O_FREE) count = kSoftmaxWarps;
       if (i >= P_FULL && i < P_FULL + kStages) count = kGroupWarps;
       if (i >= MERGE && i < MERGE + 4) count = 2;
       mbar_init(bar(i), count);
     }
     misc[1] = 0;
-    misc[2] = 0;
     mbar_fence_init();
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(misc), kTmemCols);
     tmem_relinquish();
   }
-  // Both q-blocks' exact-block bitmasks: from the routing pass, or (force modes without a
-  // mask buffer) from the force / local / sink / protected rules alone.
-  if (p.masks) {
-    for (int i = tid; i < 2 * nwords; i += kThreads) {
-      const int qb = qb0 + i / nwords;
-      sMask[i] = qb < p.nqb ? p.masks[((int64_t)bh * p.nqb + qb) * nwords + (i % nwords)] : 0u;
-    }
-  } else {
-    for (int i = warp; i < 2 * nwords; i += kThreads / 32) {
-      const int qb = qb0 + i / nwords, kb = 32 * (i % nwords) + lane;
-      const bool sel = qb < p.nqb && kb < p.nkb && route_rules(p, false, b, qb, kb);
-      const uint32_t bal = __ballot_sync(0xffffffffu, sel);
-      if (lane == 0) sMask[i] = bal;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (warp == kKWarp) {  // Q starts loading at once
-    if (p.q.idx) {
-      const RowIdx<kRows> ri = load_row_idx<kRows>(
-          p.q, p.q.idx + (int64_t)b * p.Tq + (int64_t)qb0 * kBlock, p.Tq - qb0 * kBlock, lane,
-          p.status);
-      gather_tile<D, kRows>(sQ, kQBox, p.q, ri, h, lane, bar(Q_FULL));
-    } else if (lane == 0) {
-      tma_prefetch(&tmQ);
-      mbar_expect_tx(bar(Q_FULL), L::kQTile);
-      for (int j = 0; j < D / 64; ++j)
-        tma_load_4d(sQ + j * kQBox, &tmQ, bar(Q_FULL), 64 * j, qb0 * kBlock, h, b);
-    }
+  if (warp == kKWarp) {
+    // ------------------------------------------------------------------ producer
+    // Per item: the tile list into list buffer k % 2 once the item two back has released it,
+    // Q into Q buffer k % 2 once both S issuers' MMAs of that item have completed, then the
+    // item's K and V tiles into the rings.  Slot s of the K ring is free once S_{g - kStages}
+    // has completed, slot s of the V ring once P_{g - kStages} V_{g - kStages} has; S_g itself
+    // waits for the latter, so loading K_g before that wait delays nothing.  Without gathers
+    // lane 0 alone issues the TMA loads; gathered rows are copied by the whole warp.
     if (lane == 0) {
+      if (!p.q.idx) tma_prefetch(&tmQ);
       if (!p.k.idx) {
         tma_prefetch(&tmK);
         tma_prefetch(&tmV);
@@ -293,113 +478,138 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch(&tmKC);
       tma_prefetch(&tmVC);
     }
-  }
-
-  // ---- tile list (warp 0) and exact-block counts ----
-  if (warp == 0) {
-    const uint32_t* m0 = sMask;
-    const uint32_t* m1 = sMask + nwords;
-    int n = 0;
-    const int nct = p.force == 1 ? 0 : (p.nkb + kKeys - 1) / kKeys;
-    for (int t0 = 0; t0 < nct; t0 += 32) {
-      const int t = t0 + lane;
-      bool useful = false;
-      if (t < nct) {
-        for (int wi = 2 * t; wi < 2 * t + 2 && wi < nwords; ++wi) {
-          const uint32_t v = valid_word(wi, p.nkb);
-          if ((~m0[wi] & v) || (has1 && (~m1[wi] & v))) useful = true;
+    // Items after the first come from the launch's work counter (the word after the routing
+    // masks, zeroed by the routing pass) when there is one, else round robin over the grid.
+    unsigned int* counter =
+        p.masks ? p.masks + (int64_t)p.B * p.H * p.nqb * nwords : nullptr;
+    // The next item is claimed one item ahead and its mask words are loaded while the current
+    // item's tiles stream, so that neither latency falls between two items.
+    int item = (int)blockIdx.x;
+    int next = item + (int)gridDim.x;
+    if (counter && lane == 0) next = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+    next = __shfl_sync(0xffffffffu, next, 0);
+    MaskWords mw = load_mask_words(p, item, total, nwords, lane);
+    int g = 0;  // tiles of this CTA's earlier items
+    int k_issued = 0, v_issued = 0, q_issued = 0;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int lb = k & 1;
+      if (item >= total) {  // no more work: the consumers leave their loops
+        if (k >= 2 && !warp_wait(bar(LIST_EMPTY + lb), (uint32_t)((k >> 1) - 1) & 1u,
+                                 abort_flag, p.status))
+          break;
+        if (lane == 0) {
+          misc[4 + lb] = 0xffffffffu;
+          mbar_arrive(bar(LIST_FULL + lb));
         }
+        break;
       }
-      const uint32_t bal = __ballot_sync(0xffffffffu, useful);
-      if (useful) sTiles[n + __popc(bal & ((1u << lane) - 1u))] = (int16_t)(-(t + 1));
-      n += __popc(bal);
-    }
-    int r = 0;
-    for (int w0 = 0; w0 < nwords; w0 += 32) {
-      const int wi = w0 + lane;
-      uint32_t bits = 0u;
-      if (wi < nwords) bits = m0[wi] | (has1 ? m1[wi] : 0u);
-      const int cnt = __popc(bits);
-      int incl = cnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
+      const ItemPos ip = item_pos(p, item);
+      // Q of the item first: it does not depend on the tile list.
+      if (k >= 2 && !warp_wait(bar(Q_EMPTY + lb), (uint32_t)((k >> 1) - 1) & 1u, abort_flag,
+                               p.status)) {
+        ok = false;
+        break;
       }
-      int rank = n + r + incl - cnt;
-      while (bits) {
-        const int bit = __ffs(bits) - 1;
-        bits &= bits - 1u;
-        sTiles[rank++] = (int16_t)(32 * wi + bit);
+      const uint32_t dq = sQ + (uint32_t)(lb * L::kQTile);
+      if (p.q.idx) {
+        const RowIdx<kRows> ri = load_row_idx<kRows>(
+            p.q, p.q.idx + (int64_t)ip.b * p.Tq + (int64_t)ip.qb0 * kBlock,
+            p.Tq - ip.qb0 * kBlock, lane, p.status);
+        gather_tile<D, kRows>(dq, kQBox, p.q, ri, ip.h, lane, bar(Q_FULL + lb));
+      } else if (lane == 0) {
+        mbar_expect_tx(bar(Q_FULL + lb), L::kQTile);
+        for (int j = 0; j < D / 64; ++j)
+          tma_load_4d(dq + j * kQBox, &tmQ, bar(Q_FULL + lb), 64 * j, ip.qb0 * kBlock, ip.h, ip.b);
       }
-      r += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) misc[2] = (uint32_t)(n + r);
-    if (lane < 2 && p.counts && qb0 + lane < p.nqb) {
-      int c = 0;
-      for (int i = 0; i < nwords; ++i) c += __popc(sMask[lane * nwords + i]);
-      p.counts[((int64_t)b * p.nqb + qb0 + lane) * p.H + h] = c;
-    }
-  }
-  __syncthreads();
-  const int ntiles = (int)misc[2];
-
-  if (warp == kKWarp) {
-    // ------------------------------------------------------------------ producer: K, V rings
-    // Slot s of the K ring is free once S_{i - kStages} has completed, slot s of the V ring once
-    // P_{i - kStages} V_{i - kStages} has; S_i itself waits for the latter, so loading K_i
-    // before that wait delays nothing.  Without gathers lane 0 alone runs the loop and issues
-    // TMA loads; gathered rows are copied by the whole warp.
-    int k_issued = 0, v_issued = 0;
-    if (!p.k.idx) {
+      ++q_issued;
+      // The item after next: claimed now, used two items on.
+      int next2 = next + (int)gridDim.x;
+      if (counter && lane == 0) next2 = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+      // The tile list, once the item two back has released the buffer.
+      if (k >= 2 && !warp_wait(bar(LIST_EMPTY + lb), (uint32_t)((k >> 1) - 1) & 1u, abort_flag,
+                               p.status)) {
+        ok = false;
+        break;
+      }
+      int16_t* tl = sTiles + lb * max_tiles;
+      const int ntiles = build_tile_list(p, ip, mw, sMask + lb * 2 * nwords, tl, nwords, lane);
       if (lane == 0) {
+        misc[2 + lb] = (uint32_t)ntiles;
+        misc[4 + lb] = (uint32_t)item;
+        mbar_arrive(bar(LIST_FULL + lb));
+      }
+      mw = load_mask_words(p, next, total, nwords, lane);
+      // K and V tiles of the item
+      if (!p.k.idx) {
+        if (lane == 0) {
+          for (int i = 0; i < ntiles; ++i) {
+            const int gi = g + i, s = gi % kStages;
+            const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;  // parity of the last use
+            if (gi >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), tl[i], ip.h, ip.b);
+            ++k_issued;
+            if (gi >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), tl[i], ip.h, ip.b);
+            ++v_issued;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      } else {
+        // Gathered K/V rows: the whole warp copies; a tile's 64 row indices (shared by K and
+        // V) are loaded one tile ahead.  Centroid tiles still come by TMA (lane 0), the other
+        // lanes arriving on the barrier, which counts one arrival per lane in this mode.
+        const int64_t* kvidx = p.k.idx + (int64_t)ip.b * p.Tk;
+        auto row_idx = [&](int e) {
+          RowIdx<kKeys> ri;
+          if (e >= 0) {
+            ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, p.Tk - e * kBlock, lane,
+                                     p.status);
+          } else {
+            ri.t[0] = ri.t[1] = 0;
+          }
+          return ri;
+        };
+        RowIdx<kKeys> ri = row_idx(ntiles > 0 ? tl[0] : -1);
         for (int i = 0; i < ntiles; ++i) {
-          const int s = i % kStages;
-          const uint32_t prev = (uint32_t)(i / kStages - 1) & 1u;  // parity of the last use
-          if (i >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) break;
-          load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), sTiles[i], h, b);
+          const int gi = g + i, s = gi % kStages;
+          const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;
+          const int e = tl[i];
+          if (gi >= kStages && !warp_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          if (e >= 0) gather_tile<D, kKeys>(sK + s * L::kKVTile, kKVBox, p.k, ri, ip.h, lane, bar(K_FULL + s));
+          else if (lane == 0) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, ip.h, ip.b);
+          else mbar_arrive(bar(K_FULL + s));
           ++k_issued;
-          if (i >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) break;
-          load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), sTiles[i], h, b);
+          if (gi >= kStages && !warp_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          if (e >= 0) gather_tile<D, kKeys>(sV + s * L::kKVTile, kKVBox, p.v, ri, ip.h, lane, bar(V_FULL + s));
+          else if (lane == 0) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, ip.h, ip.b);
+          else mbar_arrive(bar(V_FULL + s));
           ++v_issued;
+          if (i + 1 < ntiles) ri = row_idx(tl[i + 1]);
         }
       }
-    } else {
-      // Gathered K/V rows: the whole warp copies; a tile's 64 row indices (shared by K and V)
-      // are loaded one tile ahead.  Centroid tiles still come by TMA (lane 0), the other lanes
-      // arriving on the barrier, which counts one arrival per lane in this mode.
-      const int64_t* kvidx = p.k.idx + (int64_t)b * p.Tk;
-      auto row_idx = [&](int e) {
-        RowIdx<kKeys> ri;
-        if (e >= 0) {
-          ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, p.Tk - e * kBlock, lane,
-                                   p.status);
-        } else {
-          ri.t[0] = ri.t[1] = 0;
-        }
-        return ri;
-      };
-      RowIdx<kKeys> ri = row_idx(ntiles > 0 ? sTiles[0] : -1);
-      for (int i = 0; i < ntiles; ++i) {
-        const int s = i % kStages;
-        const uint32_t prev = (uint32_t)(i / kStages - 1) & 1u;
-        const int e = sTiles[i];
-        if (i >= kStages && !warp_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) break;
-        if (e >= 0) gather_tile<D, kKeys>(sK + s * L::kKVTile, kKVBox, p.k, ri, h, lane, bar(K_FULL + s));
-        else if (lane == 0) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, h, b);
-        else mbar_arrive(bar(K_FULL + s));
-        ++k_issued;
-        if (i >= kStages && !warp_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) break;
-        if (e >= 0) gather_tile<D, kKeys>(sV + s * L::kKVTile, kKVBox, p.v, ri, h, lane, bar(V_FULL + s));
-        else if (lane == 0) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, h, b);
-        else mbar_arrive(bar(V_FULL + s));
-        ++v_issued;
-        if (i + 1 < ntiles) ri = row_idx(sTiles[i + 1]);
-      }
-      cp_async_wait_all();  // never leave while a copy may still write shared memory
+      g += ntiles;
+      item = next;
+      next = __shfl_sync(0xffffffffu, next2, 0);
     }
+    if (p.q.idx || p.k.idx) cp_async_wait_all();  // no copy may still write shared memory
     if (lane == 0 && *abort_flag) {
-      mbar_wait_quiet(bar(Q_FULL), 0);
+      for (int j = 0; j < 2; ++j) {
+        const int n = q_issued > j ? (q_issued - j + 1) / 2 : 0;
+        if (n) mbar_wait_quiet(bar(Q_FULL + j), (uint32_t)(n - 1) & 1u);
+      }
       for (int s = 0; s < kStages; ++s) {
         int n = loads_into(k_issued, s);
         if (n) mbar_wait_quiet(bar(K_FULL + s), (uint32_t)(n - 1) & 1u);
@@ -413,25 +623,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idO = idesc_bf16(kRows, D, true);
     constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
     const uint64_t dV = smem_desc_sw128(sV, kKVBox, 1024);
-    for (int i = 0; i < ntiles; ++i) {
-      const int s = i % kStages;
-      const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-      if (!warp_wait(bar(P_FULL + s), ph, abort_flag, p.status) ||
-          !warp_wait(bar(V_FULL + s), ph, abort_flag, p.status))
-        break;
-      tc_fence_after();
-      if (p.k.idx) fence_proxy_async_smem();  // gathered V rows were written by cp.async
-      if (lane == 0) {
-        const uint64_t vd = dV + (uint64_t)s * kSlotStep;
-        const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
-        const uint32_t tO = tmem + kTmemO + (uint32_t)(128 * (i & 1));  // the tile's group
-#pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k)
-          mma_ts(tO, tP + (uint32_t)(8 * k), vd + (uint64_t)((k * 16 * 128) >> 4), idO,
-                 (i > 1 || k > 0) ? 1u : 0u);
-        mma_commit(bar(PV_DONE + s));
-      }
+    int g = 0;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int lb = k & 1;
+      if (!warp_wait(bar(LIST_FULL + lb), (uint32_t)(k >> 1) & 1u, abort_flag, p.status)) break;
+      const int item = (int)vmisc[4 + lb];
+      const int ntiles = (int)vmisc[2 + lb];
+      if (item < 0) break;
       __syncwarp();
+      if (lane == 0) mbar_arrive(bar(LIST_EMPTY + lb));
+      // The previous item's epilogue has read both O accumulators.
+      if (k >= 1 && !warp_wait(bar(O_FREE), (uint32_t)(k - 1) & 1u, abort_flag, p.status)) break;
+      for (int i = 0; i < ntiles; ++i) {
+        const int gi = g + i, s = gi % kStages;
+        const uint32_t ph = (uint32_t)(gi / kStages) & 1u;
+        if (!warp_wait(bar(P_FULL + s), ph, abort_flag, p.status) ||
+            !warp_wait(bar(V_FULL + s), ph, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (p.k.idx) fence_proxy_async_smem();  // gathered V rows were written by cp.async
+        if (lane == 0) {
+          const uint64_t vd = dV + (uint64_t)s * kSlotStep;
+          const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
+          const uint32_t tO = tmem + kTmemO + (uint32_t)(128 * (gi & 1));  // the tile's group
+          // Local tiles 0 and 1 are each group's first of the item: they start the accumulator.
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 16; ++kk)
+            mma_ts(tO, tP + (uint32_t)(8 * kk), vd + (uint64_t)((kk * 16 * 128) >> 4), idO,
+                   (i > 1 || kk > 0) ? 1u : 0u);
+          mma_commit(bar(PV_DONE + s));
+        }
+        __syncwarp();
+      }
+      g += ntiles;
     }
     if (lane == 0) {
       mma_commit(bar(DRAIN_PV));
@@ -440,38 +667,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp >= kSWarp0) {
     // ------------------------------------------------------------------ S issue (two warps)
-    const int par = warp - kSWarp0;  // tiles i with i % 2 == par
+    const int par = warp - kSWarp0;  // tiles g with g % 2 == par
     constexpr uint32_t idS = idesc_bf16(kRows, kKeys, false);
     constexpr uint64_t kSlotStep = (uint64_t)(L::kKVTile >> 4);
-    const uint64_t dQ = smem_desc_sw128(sQ, 16, 1024);
     const uint64_t dK = smem_desc_sw128(sK, 16, 1024);
-    if (warp_wait(bar(Q_FULL), 0, abort_flag, p.status)) {
+    int g = 0;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int lb = k & 1;
+      const uint32_t iph = (uint32_t)(k >> 1) & 1u;
+      if (!warp_wait(bar(LIST_FULL + lb), iph, abort_flag, p.status)) break;
+      const int item = (int)vmisc[4 + lb];
+      const int ntiles = (int)vmisc[2 + lb];
+      if (item < 0) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(LIST_EMPTY + lb));
+      if (!warp_wait(bar(Q_FULL + lb), iph, abort_flag, p.status)) break;
       if (p.q.idx) fence_proxy_async_smem();  // gathered Q rows were written by cp.async
-      for (int i = par; i < ntiles; i += 2) {
-        const int s = i % kStages;
-        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-        // P_{i - kStages} V_{i - kStages} (the last reader of the buffer) has completed, and
-        // K_i has landed.  The order matters: the two issuers run independently, and only once
-        // tile i - kStages is finished can K_FULL of this slot not still be a phase behind
+      const uint64_t dQ = smem_desc_sw128(sQ + (uint32_t)(lb * L::kQTile), 16, 1024);
+      for (int i = (par ^ g) & 1; i < ntiles; i += 2) {
+        const int gi = g + i, s = gi % kStages;
+        const uint32_t ph = (uint32_t)(gi / kStages) & 1u;
+        // P_{g - kStages} V_{g - kStages} (the last reader of the buffer) has completed, and
+        // K_g has landed.  The order matters: the two issuers run independently, and only once
+        // tile g - kStages is finished can K_FULL of this slot not still be a phase behind
         // (a parity wait on a barrier two phases behind would pass at once).
-        if (i >= kStages && !warp_wait(bar(PV_DONE + s), ph ^ 1u, abort_flag, p.status)) break;
-        if (!warp_wait(bar(K_FULL + s), ph, abort_flag, p.status)) break;
+        if (gi >= kStages && !warp_wait(bar(PV_DONE + s), ph ^ 1u, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        if (!warp_wait(bar(K_FULL + s), ph, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         if (p.k.idx) fence_proxy_async_smem();  // gathered K rows were written by cp.async
         if (lane == 0) {
           const uint64_t kd = dK + (uint64_t)s * kSlotStep;
           const uint32_t tS = tmem + kTmemS + (uint32_t)(kKeys * s);
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint64_t off = (uint64_t)(((k >> 2) * kQBox + (k & 3) * 32) >> 4);
-            const uint64_t offk = (uint64_t)(((k >> 2) * kKVBox + (k & 3) * 32) >> 4);
-            mma_ss(tS, dQ + off, kd + offk, idS, k > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t off = (uint64_t)(((kk >> 2) * kQBox + (kk & 3) * 32) >> 4);
+            const uint64_t offk = (uint64_t)(((kk >> 2) * kKVBox + (kk & 3) * 32) >> 4);
+            mma_ss(tS, dQ + off, kd + offk, idS, kk > 0 ? 1u : 0u);
           }
           mma_commit(bar(S_FULL + s));
           mma_commit(bar(K_EMPTY + s));
         }
         __syncwarp();
       }
+      // Q buffer lb is free once this issuer's MMAs of the item have completed.
+      if (ok && lane == 0) mma_commit(bar(Q_EMPTY + lb));
+      __syncwarp();
+      g += ntiles;
     }
     if (lane == 0) {
       mma_commit(bar(DRAIN_S0 + par));
@@ -483,79 +731,84 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3, grp = warp >> 2;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;  // TMEM lanes 32 quarter..
     const uint32_t tOr = tmem + kTmemO + (uint32_t)(128 * grp) + lane_base;
-    const int row = quarter * 32 + lane;
-    const int qsel = quarter >> 1;                 // lanes 0-63: qb0, lanes 64-127: qb0 + 1
-    const bool warp_rows = qsel == 0 || has1;      // the warp's q-block exists
-    const uint32_t* mymask = sMask + qsel * nwords;
+    const int qsel = quarter >> 1;  // lanes 0-63: qb0, lanes 64-127: qb0 + 1
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
-    const uint64_t six2 = f2_pack(6.f, 6.f);       // log2(64): bias of a full block's centroid
+    const uint64_t six2 = f2_pack(6.f, 6.f);  // log2(64): bias of a full block's centroid
     const int last_len = p.Tk - (p.nkb - 1) * kBlock;
     const float last_bias = log2f((float)last_len);
-    const int last_col = (p.nkb - 1) & 63;         // column of the last centroid in its group
+    const int last_col = (p.nkb - 1) & 63;  // column of the last centroid in its group
     const int last_group = (p.nkb - 1) >> 6;
-    float m_run = -INFINITY, l_run = 0.f;
+    int g = 0;
     bool ok = true;
-    int last = -1;  // this group's previous tile (its P V is the last one into O_grp)
-    for (int i = grp; ok && i < ntiles; i += 2) {
-      const int s = i % kStages;
-      // Tile metadata first: these shared-memory reads overlap the wait for S.  Every value
-      // below is warp-uniform (one q-block per warp).
-      const int entry = sTiles[i];
-      const bool centroid = entry < 0;
-      uint32_t approx0 = 0u, approx1 = 0u;  // centroid columns this q-block uses
-      int len = 0;                          // valid keys of an exact block it selected
-      if (centroid) {
-        const int t = -entry - 1;  // 2t < nwords since t <= (nkb - 1) / 64
-        if (warp_rows) {
-          approx0 = ~mymask[2 * t] & valid_word(2 * t, p.nkb);
-          if (2 * t + 1 < nwords) approx1 = ~mymask[2 * t + 1] & valid_word(2 * t + 1, p.nkb);
-        }
-      } else if (warp_rows && ((mymask[entry >> 5] >> (entry & 31)) & 1u)) {
-        len = min(kBlock, p.Tk - entry * kBlock);
-      }
-      const bool active = centroid ? (approx0 | approx1) != 0u : len > 0;
-      if (!warp_wait(bar(S_FULL + s), (uint32_t)(i / kStages) & 1u, abort_flag, p.status)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t tSr = tmem + kTmemS + (uint32_t)(kKeys * s) + lane_base;
-      if (!active) {
-        // The tile contributes nothing to these rows: P = 0, the running max and sum stay.
-        uint32_t z[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) z[j] = 0u;
-        tmem_st32(tSr, z);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(P_FULL + s));
-        last = i;
-        continue;
-      }
-      uint32_t sv[2][32];
-      tmem_ld32(tSr, sv[0]);
-      tmem_ld32(tSr + 32, sv[1]);
-      tmem_wait_ld();
-      float m_tile, k_mul;
-      if (centroid) {
-        // Centroid logits in log2 units, s * scale_log2 + log2(len), and -inf where the block is
-        // exact for this q-block (or past the last block).
-        const int t = -entry - 1;
-        if (t == last_group && last_len != kBlock) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const uint32_t approx = c ? approx1 : approx0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float bias = (32 * c + j) == last_col ? last_bias : 6.f;
-              const float v = ((approx >> j) & 1u) ? fmaf(__uint_as_float(sv[c][j]), sl2, bias)
-                                                   : -INFINITY;
-              sv[c][j] = __float_as_uint(v);
-            }
+    for (int k = 0; ok; ++k) {
+      const int lb = k & 1;
+      if (!warp_wait(bar(LIST_FULL + lb), (uint32_t)(k >> 1) & 1u, abort_flag, p.status)) break;
+      const int item = (int)vmisc[4 + lb];
+      if (item < 0) break;
+      const int ntiles = (int)vmisc[2 + lb];
+      // The warp's q-block exists (only the last pair of a head can lack its second q-block).
+      const bool warp_rows = qsel == 0 || item_pos(p, item).qb0 + 1 < p.nqb;
+      const uint32_t* mymask = sMask + (lb * 2 + qsel) * nwords;
+      const int16_t* tl = sTiles + lb * max_tiles;
+      float m_run = -INFINITY, l_run = 0.f;
+      int last = -1;  // this group's previous tile (its P V is the last one into O_grp)
+      for (int i = (grp ^ g) & 1; i < ntiles; i += 2) {
+        const int gi = g + i, s = gi % kStages;
+        // Tile metadata first: these shared-memory reads overlap the wait for S.  Every value
+        // below is warp-uniform (one q-block per warp).
+        const int entry = tl[i];
+        const bool centroid = entry < 0;
+        uint32_t approx0 = 0u, approx1 = 0u;  // centroid columns this q-block uses
+        int len = 0;                          // valid keys of an exact block it selected
+        if (centroid) {
+          const int t = -entry - 1;  // 2t < nwords since t <= (nkb - 1) / 64
+          if (warp_rows) {
+            approx0 = ~mymask[2 * t] & valid_word(2 * t, p.nkb);
+            if (2 * t + 1 < nwords) approx1 = ~mymask[2 * t + 1] & valid_word(2 * t + 1, p.nkb);
           }
-        } else {
+        } else if (warp_rows && ((mymask[entry >> 5] >> (entry & 31)) & 1u)) {
+          len = min(kBlock, p.Tk - entry * kBlock);
+        }
+        const bool active = centroid ? (approx0 | approx1) != 0u : len > 0;
+        if (!warp_wait(bar(S_FULL + s), (uint32_t)(gi / kStages) & 1u, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tSr = tmem + kTmemS + (uint32_t)(kKeys * s) + lane_base;
+        if (!active) {
+          // The tile contributes nothing to these rows: P = 0, the running max and sum stay.
+          uint32_t z[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) z[j] = 0u;
+          tmem_st32(tSr, z);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(P_FULL + s));
+          last = gi;
+          continue;
+        }
+        uint32_t sv[2][32];
+        tmem_ld32(tSr, sv[0]);
+        tmem_ld32(tSr + 32, sv[1]);
+        tmem_wait_ld();
+        float m_tile, k_mul;
+        if (centroid) {
+          // Centroid logits in log2 units, s * scale_log2 + log2(len), and -inf where the block
+          // is exact for this q-block (or past the last block).  Every full block has
+          // log2(64) = 6; a partial last block (column lc of the last group) is patched after.
+          const int t = -entry - 1;
+          const int lc = (t == last_group && last_len != kBlock) ? last_col : kKeys;
+          float raw_lc = 0.f;
+          if (lc < kKeys) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (32 * c + j == lc) raw_lc = __uint_as_float(sv[c][j]);
+          }
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const uint32_t approx = c ? approx1 : approx0;
@@ -569,149 +822,108 @@ __global__ void __launch_bounds__(kThreads, 1)
               sv[c][j + 1] = __float_as_uint(((approx >> (j + 1)) & 1u) ? v1 : -INFINITY);
             }
           }
+          if (lc < kKeys && (((lc < 32 ? approx0 : approx1) >> (lc & 31)) & 1u)) {
+            const float v = fmaf(raw_lc, sl2, last_bias);
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (32 * c + j == lc) sv[c][j] = __float_as_uint(v);
+          }
+          m_tile = row_max64(sv);
+          k_mul = 1.f;
+        } else {
+          // Exact tiles keep raw scores: max(s) * scale_log2 equals max(s * scale_log2) bit for
+          // bit (the scale is positive) and the scale is folded into the exponent's FMA.
+          if (len < kBlock) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (32 * c + j >= len) sv[c][j] = __float_as_uint(-INFINITY);
+          }
+          m_tile = row_max64(sv) * sl2;
+          k_mul = sl2;
         }
-        m_tile = row_max64(sv);
-        k_mul = 1.f;
-      } else {
-        // Exact tiles keep raw scores: max(s) * scale_log2 equals max(s * scale_log2) bit for
-        // bit (the scale is positive) and the scale is folded into the exponent's FMA.
-        if (len < kBlock) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (32 * c + j >= len) sv[c][j] = __float_as_uint(-INFINITY);
+        // Lazy rescaling: the running max only moves when a row's max grows by more than 8
+        // (a factor 256), so P stays <= 256 and O is rarely touched; O and l share the max.
+        const float m_new = fmaxf(m_run, m_tile);
+        bool need = false;
+        float alpha = 1.f;
+        if (m_run == -INFINITY) {
+          m_run = m_new;  // nothing accumulated yet: O and l are zero for this row
+        } else if (m_new > m_run + 8.f) {
+          need = true;
+          alpha = fast_exp2(m_run - m_new);
+          l_run *= alpha;  // before this tile's sum, which uses the new max
+          m_run = m_new;
         }
-        m_tile = row_max64(sv) * sl2;
-        k_mul = sl2;
-      }
-      // Lazy rescaling: the running max only moves when a row's max grows by more than 8
-      // (a factor 256), so P stays <= 256 and O is rarely touched; O and l share the max.
-      const float m_new = fmaxf(m_run, m_tile);
-      bool need = false;
-      float alpha = 1.f;
-      if (m_run == -INFINITY) {
-        m_run = m_new;  // nothing accumulated yet: O and l are zero for this row
-      } else if (m_new > m_run + 8.f) {
-        need = true;
-        alpha = fast_exp2(m_run - m_new);
-        l_run *= alpha;  // before this tile's sum, which uses the new max
-        m_run = m_new;
-      }
-      const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      // p = exp2(s * k_mul - m_use), two lanes per FMA; sums in four packed accumulators.
-      const uint64_t kmul2 = f2_pack(k_mul, k_mul), negm2 = f2_pack(-m_use, -m_use);
-      uint64_t acc[4];
+        const float m_use = m_run == -INFINITY ? 0.f : m_run;
+        // p = exp2(s * k_mul - m_use), two lanes per FMA; sums in four packed accumulators.
+        const uint64_t kmul2 = f2_pack(k_mul, k_mul), negm2 = f2_pack(-m_use, -m_use);
+        uint64_t acc[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] = 0ull;
+        for (int j = 0; j < 4; ++j) acc[j] = 0ull;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          float x0, x1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][j]), __uint_as_float(sv[c][j + 1])),
-                           kmul2, negm2),
-                    x0, x1);
-          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          acc[(j >> 1) & 3] = f2_add(acc[(j >> 1) & 3], f2_pack(p0, p1));
-          pk[j / 2] = pack_bf16(p0, p1);
-        }
-        tmem_st16(tSr + (uint32_t)(16 * c), pk);  // P over the first 32 columns of the buffer
-      }
-      {
-        const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
-        float lo, hi;
-        f2_unpack(f2_add(a01, a23), lo, hi);
-        l_run += lo + hi;
-      }
-      if (__any_sync(0xffffffffu, need)) {
-        // O_grp may only be touched once the group's previous P V has completed (the P V issue
-        // is in order); P_i V_i is not issued before this group arrives on P_FULL below.
-        if (!warp_wait(bar(PV_DONE + last % kStages), (uint32_t)(last / kStages) & 1u,
-                       abort_flag, p.status)) {
-          tmem_wait_st();
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint64_t a2 = f2_pack(alpha, alpha);
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tOr + 32 * c, o);
-          tmem_wait_ld();
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            float y0, y1;
-            f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), a2), y0, y1);
-            o[j] = __float_as_uint(y0);
-            o[j + 1] = __float_as_uint(y1);
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][j]), __uint_as_float(sv[c][j + 1])),
+                             kmul2, negm2),
+                      x0, x1);
+            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            acc[(j >> 1) & 3] = f2_add(acc[(j >> 1) & 3], f2_pack(p0, p1));
+            pk[j / 2] = pack_bf16(p0, p1);
           }
-          tmem_st32(tOr + 32 * c, o);
+          tmem_st16(tSr + (uint32_t)(16 * c), pk);  // P over the first 32 columns of the buffer
         }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(P_FULL + s));
-      last = i;
-    }
-    // ---- epilogue: merge the two groups' softmaxes, O / l -> BF16 ----
-    if (ok && last >= 0)
-      ok = warp_wait(bar(PV_DONE + last % kStages), (uint32_t)(last / kStages) & 1u, abort_flag,
-                     p.status);
-    const float m_me = last >= 0 ? m_run : -INFINITY;
-    if (ok) {  // the partner warp (same lanes, other group) is warp ^ 4
-      sMerge[(warp * 2) * 32 + lane] = m_me;
-      sMerge[(warp * 2 + 1) * 32 + lane] = l_run;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(MERGE + quarter));
-      ok = warp_wait(bar(MERGE + quarter), 0, abort_flag, p.status);
-    }
-    if (ok) {
-      tc_fence_after();
-      const float m_o = sMerge[((warp ^ 4) * 2) * 32 + lane];
-      const float l_o = sMerge[((warp ^ 4) * 2 + 1) * 32 + lane];
-      const float m0 = grp == 0 ? m_me : m_o, m1 = grp == 0 ? m_o : m_me;
-      const float l0 = grp == 0 ? l_run : l_o, l1 = grp == 0 ? l_o : l_run;
-      const float m = fmaxf(m0, m1);
-      const float f0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
-      const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
-      const float inv = 1.f / (l0 * f0 + l1 * f1);
-      // A group without tiles never initialised its accumulator: its share is skipped.
-      const bool has0 = ntiles >= 1, has1t = ntiles >= 2;
-      const int grow = qb0 * kBlock + row;
-      // This warp writes head dims [grp * D / 2, (grp + 1) * D / 2) of its 32 rows.
-      __nv_bfloat16* dst = p.out + (((int64_t)b * p.Tq + grow) * p.H + h) * D + grp * (D / 2);
+        {
+          const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+          float lo, hi;
+          f2_unpack(f2_add(a01, a23), lo, hi);
+          l_run += lo + hi;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          // O_grp may only be touched once the group's previous P V has completed (the P V
+          // issue is in order); P_g V_g is not issued before this group arrives on P_FULL below.
+          if (!warp_wait(bar(PV_DONE + last % kStages), (uint32_t)(last / kStages) & 1u,
+                         abort_flag, p.status)) {
+            tmem_wait_st();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll 1
-      for (int c = 0; c < D / 64; ++c) {
-        const uint32_t col = (uint32_t)(grp * (D / 2) + 32 * c);
-        uint32_t o0[32], o1[32];
-        if (has0) tmem_ld32(tmem + kTmemO + lane_base + col, o0);
-        if (has1t) tmem_ld32(tmem + kTmemO + 128 + lane_base + col, o1);
-        tmem_wait_ld();
-        if (grow < p.Tq) {
-          uint4 v4[4];
-          uint32_t* w32 = reinterpret_cast<uint32_t*>(v4);
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tOr + 32 * c, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float a0 = 0.f, a1 = 0.f;
-            if (has0) {
-              a0 = __uint_as_float(o0[2 * j]) * f0;
-              a1 = __uint_as_float(o0[2 * j + 1]) * f0;
+            for (int j = 0; j < 32; j += 2) {
+              float y0, y1;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), a2), y0, y1);
+              o[j] = __float_as_uint(y0);
+              o[j + 1] = __float_as_uint(y1);
             }
-            if (has1t) {
-              a0 = fmaf(__uint_as_float(o1[2 * j]), f1, a0);
-              a1 = fmaf(__uint_as_float(o1[2 * j + 1]), f1, a1);
-            }
-            w32[j] = pack_bf16(a0 * inv, a1 * inv);
+            tmem_st32(tOr + 32 * c, o);
           }
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) d4[j] = v4[j];
         }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(P_FULL + s));
+        last = gi;
       }
+      if (!ok) break;
+      // ---- item epilogue ----
+      if (!item_epilogue<D>(tmem, bar0, warp, lane, k, last, m_run, l_run, ntiles, g,
+                            (int)vmisc[4 + lb], sMerge, abort_flag, p.status, p.out, p.Tq, p.H,
+                            p.nqb, p.q_sink_blocks, p.B))
+        break;
+      g += ntiles;
     }
   }
 
@@ -796,8 +1008,14 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
   err = cudaFuncSetAttribute(attn_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
   if (err != cudaSuccess) return err;
-  const int64_t ctas = (int64_t)((p.nqb + 1) / 2) * p.B * p.H;
-  if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
+  // Persistent grid: one CTA per SM, each working through items until none are left.
+  const int64_t items = (int64_t)((p.nqb + 1) / 2) * p.B * p.H;
+  if (items > 0x7fff0000) return cudaErrorInvalidValue;
+  int dev = 0, sms = 0;
+  err = cudaGetDevice(&dev);
+  if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (err != cudaSuccess) return err;
+  const int64_t ctas = items < sms ? items : sms;
   attn_sm100_kernel<D><<<(unsigned)ctas, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
   return cudaGetLastError();
 }

@@ -78,7 +78,7 @@ Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   L.cutoff = off;
   off = align256(off + B * H * nqb * 4);
   L.masks = off;
-  off = align256(off + B * H * nqb * cdiv(nkb, 32) * 4);
+  off = align256(off + B * H * nqb * cdiv(nkb, 32) * 4 + 4);  // + the work counter
   L.total = off;
   return L;
 }

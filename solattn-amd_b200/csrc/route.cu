@@ -8,7 +8,8 @@
 // with exactly the arithmetic of common.cuh:routing_dot (eight partial sums over d = 8i + j,
 // __fmul_rn / __fadd_rn, combined pairwise), so the decisions are bit-identical to the
 // per-CTA routing of the mma.sync kernel.  One ballot per q-block per 32 key blocks gives a
-// mask word: masks[((b * H + h) * nqb + qb) * nwords + kb / 32], bit kb % 32.
+// mask word: masks[((b * H + h) * nqb + qb) * nwords + kb / 32], bit kb % 32.  The word after
+// the last mask word is the fused attention kernel's work counter; the pass zeroes it.
 #include "common.cuh"
 
 namespace solattn {
@@ -27,6 +28,8 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   const int qb_lo = blockIdx.x * kRouteQB;
   const int nq = min(kRouteQB, p.nqb - qb_lo);
   const int nwords = (p.nkb + 31) / 32;
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    p.masks[(int64_t)p.B * p.H * p.nqb * nwords] = 0u;
   for (int i = threadIdx.x; i < kRouteQB * D; i += kRouteThreads) {
     const int j = i / D;
     sq[j][i % D] =
@@ -48,7 +51,6 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   // Warp-uniform loop over 32-block words.
   for (int w = threadIdx.x >> 5; w < nwords; w += kRouteThreads / 32) {
     const int kb = 32 * w + lane;
-    const int kbc = kb < p.nkb ? kb : p.nkb - 1;  // clamped: every address stays in range
     float part[kRouteQB][8];
 #pragma unroll
     for (int j = 0; j < kRouteQB; ++j)

@@ -48,8 +48,10 @@ class Stages:
         self.out = torch.empty((B, Tq, H, D), dtype=bf16, device=dev)
         self.counts = torch.full((B, self.nqb, H), -1, dtype=torch.int32, device=dev) if counts else None
         # Routing decisions [B, H, nqb, ceil(nkb/32)] (bit kb % 32 of word kb / 32), written by
-        # the attention call's routing pass.
-        self.mask = torch.zeros((B, H, self.nqb, (self.nkb + 31) // 32), dtype=torch.int32, device=dev)
+        # the attention call's routing pass, followed by the attention kernel's work counter.
+        nw = (self.nkb + 31) // 32
+        self._mask_words = torch.zeros(B * H * self.nqb * nw + 1, dtype=torch.int32, device=dev)
+        self.mask = self._mask_words[:-1].view(B, H, self.nqb, nw)
 
     def _strides(self, x):
         return (0, x.stride(0), x.stride(1)) if self.indexed else (x.stride(0), x.stride(1), x.stride(2))
