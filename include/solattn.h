@@ -150,6 +150,38 @@ SOLATTN_API int solattn_sol_forward(const void* q, const void* k, const void* v,
                         void* out, int32_t* counts, void* stream);
 
 /*
+ * solattn_sol_forward for indexed inputs that writes each query row's output straight to its
+ * original row: `out` is an NHD [out_rows, H, D] BF16 tensor (rows of H*D elements) and query
+ * row t of window b goes to out[q_idx[b*Tq + t]]; rows named by no window are left untouched.
+ * Replaces the caller-side scatter `out[plan.rows] = result` of the reference's VDN adapter
+ * (integrations/vdn.py:54-71), and with it the [B, Tq, H, D] intermediate.  Requires q_idx;
+ * windows that name the same row race on it.  Row indices outside [0, out_rows) are reported
+ * through the status word and skipped.
+ */
+SOLATTN_API int solattn_sol_forward_scatter(const void* q, const void* k, const void* v,
+                        int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                        int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                        int64_t k_sB, int64_t k_sT, int64_t k_sH,
+                        int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                        const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                        const uint8_t* protect,
+                        float scale, float beta, int local, int kv_sink_blocks,
+                        int q_sink_blocks, void* workspace, int64_t workspace_bytes,
+                        void* out, int64_t out_rows, int32_t* counts, void* stream);
+
+/*
+ * Dense attention of a subset of query rows against all keys, written in place: for each
+ * i < n_rows, out[rows[i]] = softmax(q[rows[i]] . k^T * scale) . v over all N keys, with q, k,
+ * v and out NHD [N, H, D] BF16 (element strides q_sT/q_sH etc.; the head dimension is
+ * contiguous).  The VDN adapter's dense global-query step (`out[rows] = dense(q[rows], k, v)`,
+ * integrations/vdn.py:58-63) without the gathered copy of Q or the scatter.  Needs no workspace.
+ */
+SOLATTN_API int solattn_dense_rows(const void* q, const void* k, const void* v,
+                  const int64_t* rows, int64_t n_rows, int64_t N, int64_t H, int64_t D,
+                  int64_t q_sT, int64_t q_sH, int64_t k_sT, int64_t k_sH,
+                  int64_t v_sT, int64_t v_sH, float scale, void* out, void* stream);
+
+/*
  * Dense noncausal attention over all keys (BF16 QK/PV, FP32 softmax).  Replaces
  * `launch_dense`/`_dense` (kernels.py:67-98, 193-200); implemented as the all-exact route
  * of the fused kernel, so it needs no workspace.

@@ -307,7 +307,15 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
       asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];\n"
                    : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
                    : "r"(a));
-      __nv_bfloat16* dst = p.out + (((int64_t)b * p.Tq + q0 + r) * p.H + h) * D + chunk * 8;
+      int64_t orow = (int64_t)b * p.Tq + q0 + r;
+      if (p.out_idx) {  // scatter: output row out_idx[b * Tq + t]
+        orow = __ldg(p.out_idx + orow);
+        if (orow < 0 || orow >= p.out_rows) {
+          report(p.status, kStatusBadIndex);
+          continue;
+        }
+      }
+      __nv_bfloat16* dst = p.out + (orow * p.H + h) * D + chunk * 8;
       *reinterpret_cast<uint4*>(dst) = val;
     }
   }

@@ -337,7 +337,8 @@ template <int D>
 __device__ __forceinline__ bool item_epilogue(uint32_t tmem, uint32_t bar0, int warp, int lane, int k,
                                            int last, float m_run, float l_run, int ntiles, int g,
                                            int item, float* sMerge, volatile int* abort_flag,
-                                           int32_t* status, __nv_bfloat16* out, int Tq, int H,
+                                           int32_t* status, __nv_bfloat16* out,
+                                           const int64_t* out_idx, int64_t out_rows, int Tq, int H,
                                            int nqb, int q_sink_blocks, int B) {
   auto bar = [bar0](int i) { return bar0 + 8u * (uint32_t)i; };
   const int quarter = warp & 3, grp = warp >> 2, lb = k & 1;
@@ -366,8 +367,18 @@ __device__ __forceinline__ bool item_epilogue(uint32_t tmem, uint32_t bar0, int 
   const bool has1 = ntiles >= 2 || (ntiles == 1 && (g & 1) == 1);
   const ItemPos ip = item_pos(item, nqb, q_sink_blocks, B, H);
   const int grow = ip.qb0 * kBlock + quarter * 32 + lane;
-  // This warp writes head dims [grp * D / 2, (grp + 1) * D / 2) of its 32 rows.
-  __nv_bfloat16* dst = out + (((int64_t)ip.b * Tq + grow) * H + ip.h) * D + grp * (D / 2);
+  // This warp writes head dims [grp * D / 2, (grp + 1) * D / 2) of its 32 rows: row grow of
+  // batch b, or (scatter) output row out_idx[b * Tq + grow].
+  bool store = grow < Tq;
+  int64_t orow = (int64_t)ip.b * Tq + grow;
+  if (out_idx && store) {
+    orow = __ldg(out_idx + orow);
+    if (orow < 0 || orow >= out_rows) {
+      report(status, kStatusBadIndex);
+      store = false;
+    }
+  }
+  __nv_bfloat16* dst = out + (orow * H + ip.h) * D + grp * (D / 2);
 #pragma unroll 1
   for (int c = 0; c < D / 32; ++c) {  // 16 columns at a time
     const uint32_t col = (uint32_t)(grp * (D / 2) + 16 * c);
@@ -381,7 +392,7 @@ __device__ __forceinline__ bool item_epilogue(uint32_t tmem, uint32_t bar0, int 
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(O_FREE));
     }
-    if (grow < Tq) {
+    if (store) {
       uint32_t w[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -920,8 +931,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // ---- item epilogue ----
       if (!item_epilogue<D>(tmem, bar0, warp, lane, k, last, m_run, l_run, ntiles, g,
-                            (int)vmisc[4 + lb], sMerge, abort_flag, p.status, p.out, p.Tq, p.H,
-                            p.nqb, p.q_sink_blocks, p.B))
+                            (int)vmisc[4 + lb], sMerge, abort_flag, p.status, p.out, p.out_idx,
+                            p.out_rows, p.Tq, p.H, p.nqb, p.q_sink_blocks, p.B))
         break;
       g += ntiles;
     }

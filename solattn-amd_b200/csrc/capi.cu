@@ -166,18 +166,26 @@ int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int
                                     cutoff, static_cast<cudaStream_t>(stream)));
 }
 
-int solattn_attention(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
-                      int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH,
-                      int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT,
-                      int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
-                      const void* kc, const void* vc, const float* qc, const float* cutoff,
-                      const uint8_t* protect, float scale, int force, int local,
-                      int kv_sink_blocks, int q_sink_blocks, void* out, int32_t* counts,
-                      int32_t* status, uint32_t* masks, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// solattn_attention with an optional output row index (out_idx [B, Tq], out_rows rows of an NHD
+// output); see solattn_sol_forward_scatter.
+int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                   int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                   int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT,
+                   int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                   const void* kc, const void* vc, const float* qc, const float* cutoff,
+                   const uint8_t* protect, float scale, int force, int local,
+                   int kv_sink_blocks, int q_sink_blocks, void* out, const int64_t* out_idx,
+                   int64_t out_rows, int32_t* counts, int32_t* status, uint32_t* masks,
+                   void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (!q || !k || !v || !kc || !vc || !out) return SOLATTN_ERR_ARG;
   if (force == SOLATTN_FORCE_THRESHOLD && !masks) return SOLATTN_ERR_ARG;
+  if (out_idx && out_rows <= 0) return SOLATTN_ERR_ARG;
   if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
   if (force < 0 || force > 2 || (force == 0 && (!qc || !cutoff))) return SOLATTN_ERR_ARG;
   if (!(scale > 0.f) || !isfinite(scale) || kv_sink_blocks < 0 || q_sink_blocks < 0)
@@ -198,6 +206,8 @@ int solattn_attention(const void* q, const void* k, const void* v, int64_t B, in
   p.cutoff = cutoff;
   p.protect = protect;
   p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_idx = out_idx;
+  p.out_rows = out_idx ? out_rows : 0;
   p.counts = counts;
   p.status = status;
   p.masks = masks;
@@ -216,13 +226,14 @@ int solattn_attention(const void* q, const void* k, const void* v, int64_t B, in
   return from_cuda(launch_attention(p, (int)D, static_cast<cudaStream_t>(stream)));
 }
 
-int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
-                        int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT,
-                        int64_t q_sH, int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB,
-                        int64_t v_sT, int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx,
-                        int64_t idx_rows, const uint8_t* protect, float scale, float beta, int local,
-                        int kv_sink_blocks, int q_sink_blocks, void* workspace,
-                        int64_t workspace_bytes, void* out, int32_t* counts, void* stream) {
+int sol_forward_impl(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                     int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                     int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT,
+                     int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                     const uint8_t* protect, float scale, float beta, int local,
+                     int kv_sink_blocks, int q_sink_blocks, void* workspace,
+                     int64_t workspace_bytes, void* out, const int64_t* out_idx, int64_t out_rows,
+                     int32_t* counts, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (isnan(beta) || !workspace) return SOLATTN_ERR_ARG;
@@ -260,12 +271,72 @@ int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, 
                            reinterpret_cast<float*>(ws + L.var), cutoff, stream);
     if (rc) return rc;
   }
-  return solattn_attention(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
-                           v_sT, v_sH, q_idx, kv_idx, idx_rows, kc, vc,
-                           force == SOLATTN_FORCE_THRESHOLD ? qc : nullptr,
-                           force == SOLATTN_FORCE_THRESHOLD ? cutoff : nullptr, protect, scale,
-                           force, local, kv_sink_blocks, q_sink_blocks, out, counts, status,
-                           reinterpret_cast<uint32_t*>(ws + L.masks), stream);
+  return attention_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
+                        v_sT, v_sH, q_idx, kv_idx, idx_rows, kc, vc,
+                        force == SOLATTN_FORCE_THRESHOLD ? qc : nullptr,
+                        force == SOLATTN_FORCE_THRESHOLD ? cutoff : nullptr, protect, scale, force,
+                        local, kv_sink_blocks, q_sink_blocks, out, out_idx, out_rows, counts,
+                        status, reinterpret_cast<uint32_t*>(ws + L.masks), stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int solattn_attention(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                      int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                      int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT,
+                      int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                      const void* kc, const void* vc, const float* qc, const float* cutoff,
+                      const uint8_t* protect, float scale, int force, int local,
+                      int kv_sink_blocks, int q_sink_blocks, void* out, int32_t* counts,
+                      int32_t* status, uint32_t* masks, void* stream) {
+  return attention_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT,
+                        v_sH, q_idx, kv_idx, idx_rows, kc, vc, qc, cutoff, protect, scale, force,
+                        local, kv_sink_blocks, q_sink_blocks, out, nullptr, 0, counts, status,
+                        masks, stream);
+}
+
+int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                        int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT,
+                        int64_t q_sH, int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB,
+                        int64_t v_sT, int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx,
+                        int64_t idx_rows, const uint8_t* protect, float scale, float beta, int local,
+                        int kv_sink_blocks, int q_sink_blocks, void* workspace,
+                        int64_t workspace_bytes, void* out, int32_t* counts, void* stream) {
+  return sol_forward_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
+                          v_sT, v_sH, q_idx, kv_idx, idx_rows, protect, scale, beta, local,
+                          kv_sink_blocks, q_sink_blocks, workspace, workspace_bytes, out, nullptr,
+                          0, counts, stream);
+}
+
+int solattn_sol_forward_scatter(const void* q, const void* k, const void* v, int64_t B,
+                                int64_t Tq, int64_t Tk, int64_t H, int64_t D, int64_t q_sB,
+                                int64_t q_sT, int64_t q_sH, int64_t k_sB, int64_t k_sT,
+                                int64_t k_sH, int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                                const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                                const uint8_t* protect, float scale, float beta, int local,
+                                int kv_sink_blocks, int q_sink_blocks, void* workspace,
+                                int64_t workspace_bytes, void* out, int64_t out_rows,
+                                int32_t* counts, void* stream) {
+  if (!q_idx || out_rows <= 0) return SOLATTN_ERR_ARG;
+  return sol_forward_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
+                          v_sT, v_sH, q_idx, kv_idx, idx_rows, protect, scale, beta, local,
+                          kv_sink_blocks, q_sink_blocks, workspace, workspace_bytes, out, q_idx,
+                          out_rows, counts, stream);
+}
+
+int solattn_dense_rows(const void* q, const void* k, const void* v, const int64_t* rows,
+                       int64_t n_rows, int64_t N, int64_t H, int64_t D, int64_t q_sT,
+                       int64_t q_sH, int64_t k_sT, int64_t k_sH, int64_t v_sT, int64_t v_sH,
+                       float scale, void* out, void* stream) {
+  if (!rows || n_rows <= 0 || N <= 0) return SOLATTN_ERR_ARG;
+  // One batch: the n_rows gathered query rows against all N keys (all-exact route, so the
+  // K/V pointers stand in for the pooled statistics), written to out[rows].
+  return attention_impl(q, k, v, 1, n_rows, N, H, D, 0, q_sT, q_sH, 0, k_sT, k_sH, 0, v_sT, v_sH,
+                        rows, nullptr, N, k, v, nullptr, nullptr, nullptr, scale,
+                        SOLATTN_FORCE_ALL, -1, 0, 0, out, rows, N, nullptr, nullptr, nullptr,
+                        stream);
 }
 
 int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,

@@ -31,7 +31,10 @@ struct AttnParams {
   const float* qc;          // [B, H, nqb, D]
   const float* cutoff;      // [B, H, nqb]
   const uint8_t* protect;   // [B, nqb, nkb] or nullptr
-  __nv_bfloat16* out;       // [B, Tq, H, D]
+  __nv_bfloat16* out;       // [B, Tq, H, D], or NHD [out_rows, H, D] when out_idx is set
+  const int64_t* out_idx;   // optional output rows [B, Tq]: row t of batch b goes to
+                            // out[out_idx[b * Tq + t]] (the indexed forms' scatter), else nullptr
+  int64_t out_rows;         // rows of `out` when out_idx is set (bounds for out_idx)
   int32_t* counts;          // [B, nqb, H] or nullptr
   int32_t* status;          // device status word or nullptr
   uint32_t* masks;          // [B, H, nqb, ceil(nkb/32)] routing bitmask: written by route.cu

@@ -82,11 +82,13 @@ def _strides(x: torch.Tensor, indexed: bool):
 
 
 def launch_sol(q, k, v, scale, beta, local, kv_sink, q_sink, stats, protection=None,
-               rows=None, keys=None):
+               rows=None, keys=None, out=None):
     """Allocate outputs + workspace and run the all-in forward (``kernels.py:203-225``).
 
     BTHD inputs, or NHD inputs with gather indices ``rows`` [W, nq] / ``keys`` [W, nk]
-    (then the logical shape is B=W, Tq=nq, Tk=nk).  Returns (out, counts).
+    (then the logical shape is B=W, Tq=nq, Tk=nk).  With ``out`` (indexed only: an NHD tensor
+    like ``q``) each query row's output is written to ``out[rows[w, i]]`` instead of a fresh
+    [W, nq, H, D] tensor.  Returns (out, counts).
     """
     indexed = rows is not None
     # The kernels need 16-byte-aligned rows; other positive strides are made contiguous first.
@@ -107,19 +109,25 @@ def launch_sol(q, k, v, scale, beta, local, kv_sink, q_sink, stats, protection=N
         raise _lib.SolAttnError("unsupported shape for libsolattn")
     workspace = torch.empty(total + 256, dtype=torch.uint8, device=q.device)
     ws_ptr = (workspace.data_ptr() + 255) // 256 * 256
-    out = torch.empty(out_shape, dtype=torch.bfloat16, device=q.device)
+    scatter = out is not None
+    if not scatter:
+        out = torch.empty(out_shape, dtype=torch.bfloat16, device=q.device)
     counts = torch.empty((B, nqb, H), dtype=torch.int32, device=q.device)
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    rc = L.solattn_sol_forward(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), B, Tq, Tk, H, D,
-        *_strides(q, indexed), *_strides(k, indexed), *_strides(v, indexed),
-        rows.data_ptr() if indexed else None, keys.data_ptr() if indexed else None,
-        q.shape[0] if indexed else 0,
-        protection.data_ptr() if protection is not None else None,
-        float(scale), float(beta), int(local), (kv_sink + BLOCK - 1) // BLOCK,
-        (q_sink + BLOCK - 1) // BLOCK, ws_ptr, total, out.data_ptr(),
-        counts.data_ptr() if stats else None, stream)
-    _lib.check(rc, "solattn_sol_forward")
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), B, Tq, Tk, H, D,
+            *_strides(q, indexed), *_strides(k, indexed), *_strides(v, indexed),
+            rows.data_ptr() if indexed else None, keys.data_ptr() if indexed else None,
+            q.shape[0] if indexed else 0,
+            protection.data_ptr() if protection is not None else None,
+            float(scale), float(beta), int(local), (kv_sink + BLOCK - 1) // BLOCK,
+            (q_sink + BLOCK - 1) // BLOCK, ws_ptr, total, out.data_ptr())
+    if scatter:
+        rc = L.solattn_sol_forward_scatter(*args, out.shape[0],
+                                           counts.data_ptr() if stats else None, stream)
+        _lib.check(rc, "solattn_sol_forward_scatter")
+    else:
+        rc = L.solattn_sol_forward(*args, counts.data_ptr() if stats else None, stream)
+        _lib.check(rc, "solattn_sol_forward")
     if _CHECK_STATUS:
         check_status(ws_ptr + offs["status"], stream)
     return out, counts
@@ -150,6 +158,51 @@ def dense_attention(q, k, v, *, scale=None):
                                        *_strides(v, False), float(scale), out.data_ptr(), stream)
         _lib.check(rc, "solattn_dense")
         return out
+
+
+def dense_attention_rows(q, k, v, rows, *, scale=None, out=None):
+    """Dense attention of the query rows ``rows`` against all keys, written to ``out[rows]``.
+
+    ``q``, ``k``, ``v`` are NHD [N, H, D] BF16 CUDA tensors of one sequence and ``rows`` a 1-D
+    int64 tensor of row indices on their device.  This is the VDN adapter's dense step for
+    global queries (``out[rows] = dense(q[rows], k, v, scale)``,
+    ``integrations/vdn.py:58-63``) without the gathered copy of Q or the scatter; it has no
+    counterpart in the reference package.  ``out`` (NHD like ``q``, contiguous) receives the
+    rows and is returned; when omitted a new uninitialised tensor like ``q`` is used, as the
+    adapter's ``torch.empty_like(q)``.  Rows outside [0, N) are reported by the kernel's status
+    word and skipped.
+    """
+    if any(t.ndim != 3 for t in (q, k, v)) or q.shape != k.shape or k.shape != v.shape:
+        raise ValueError("Q/K/V must have matching NHD shapes")
+    scale = _validate(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), scale)
+    if (not isinstance(rows, torch.Tensor) or rows.dtype != torch.int64 or rows.ndim != 1
+            or rows.numel() == 0 or rows.device != q.device):
+        raise ValueError("rows must be a nonempty 1-D int64 tensor on the Q/K/V device")
+    out = _check_out(out, q)
+    with torch.no_grad(), torch.cuda.device(q.device):
+        q, k, v = (x if _aligned(x) else x.contiguous() for x in (q, k, v))
+        rows = rows.contiguous()
+        if out is None:
+            out = torch.empty_like(q, memory_format=torch.contiguous_format)
+        N, H, D = q.shape
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = _lib.load().solattn_dense_rows(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), rows.data_ptr(), rows.numel(), N, H, D,
+            q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+            float(scale), out.data_ptr(), stream)
+        _lib.check(rc, "solattn_dense_rows")
+        return out
+
+
+def _check_out(out, q):
+    """Validate a caller-provided NHD output tensor shaped like ``q``."""
+    if out is None:
+        return None
+    if (not isinstance(out, torch.Tensor) or out.dtype != torch.bfloat16
+            or out.device != q.device or tuple(out.shape) != tuple(q.shape)
+            or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous BF16 tensor shaped like Q on its device")
+    return out
 
 
 def sol_attention(q, k, v, *, beta=1.0, scale=None, local_blocks=1,

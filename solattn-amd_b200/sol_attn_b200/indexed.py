@@ -14,7 +14,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .attention import SolStats, _nonnegative_integer, _validate, launch_sol
+from .attention import SolStats, _check_out, _nonnegative_integer, _validate, launch_sol
 
 BLOCK = 64
 
@@ -93,11 +93,16 @@ class IndexedPlan:
                            self.protected_blocks.to(device), self.sequence_length)
 
 
-def sol_attention_indexed(q, k, v, plan, *, beta=1.0, scale=None, return_stats=False):
+def sol_attention_indexed(q, k, v, plan, *, beta=1.0, scale=None, return_stats=False,
+                          out=None):
     """BF16 NHD inputs -> [windows, query_rows, heads, D] output (``indexed.py:69-104``).
 
     Includes pooling, thresholds and attention over the plan's gathered rows. Plan creation
-    and transfer are explicit one-time setup costs. Does not scatter output.
+    and transfer are explicit one-time setup costs. Does not scatter output, unless ``out``
+    is given (an extension: a contiguous BF16 NHD tensor shaped like ``q``): then each query
+    row's output goes straight to ``out[plan.rows[w, i]]`` - the caller-side
+    ``out[plan.rows] = result`` of the reference's VDN adapter - and ``out`` is returned; rows
+    no window names keep their contents, and windows naming the same row race on it.
     """
     if any(t.ndim != 3 for t in (q, k, v)) or q.shape != k.shape or k.shape != v.shape:
         raise ValueError("Indexed Q/K/V must have matching NHD shapes")
@@ -119,9 +124,10 @@ def sol_attention_indexed(q, k, v, plan, *, beta=1.0, scale=None, return_stats=F
     beta = float(beta)
     if math.isnan(beta):
         raise ValueError("beta must not be NaN")
+    out = _check_out(out, q)
     with torch.no_grad(), torch.cuda.device(q.device):
         out, counts = launch_sol(q, k, v, scale, beta, -1, 0, 0, return_stats,
-                                 plan.protected_blocks, rows=plan.rows, keys=plan.keys)
+                                 plan.protected_blocks, rows=plan.rows, keys=plan.keys, out=out)
     if return_stats:
         return out, SolStats(counts, (plan.keys.shape[1] + 63) // 64)
     return out

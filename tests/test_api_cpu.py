@@ -54,3 +54,16 @@ def test_sink_and_beta_validation_is_reached_only_on_device():
     q, k, v = workloads.reference_fixture()
     with pytest.raises(ValueError):
         sol_attention(q, k, v, beta=math.nan)
+
+
+def test_scatter_and_dense_rows_reject_bad_arguments_on_cpu():
+    from sol_attn_b200 import dense_attention_rows
+    q = torch.zeros((100, 2, 64), dtype=torch.bfloat16)
+    rows = torch.arange(10)
+    with pytest.raises(ValueError, match="B200"):
+        dense_attention_rows(q, q, q, rows)
+    with pytest.raises(ValueError, match="NHD"):
+        dense_attention_rows(q, q[:50], q, rows)
+    plan = IndexedPlan.create(torch.arange(64)[None], torch.arange(64)[None], 100)
+    with pytest.raises(ValueError, match="B200"):
+        sol_attention_indexed(q, q, q, plan, out=torch.zeros_like(q))

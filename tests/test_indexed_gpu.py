@@ -62,3 +62,47 @@ def test_indexed_routing_and_pooling_bit_identical():
     sel = kernel_order.route(qc, kc, r["cut"].cpu().numpy(), r["scale"], 0, -1, 0, 0,
                              p.protected_blocks.numpy())
     np.testing.assert_array_equal(r["mask"].cpu().numpy().view(np.uint32), kernel_order.pack_mask(sel))
+
+
+def test_indexed_scatter_writes_rows_in_place():
+    """``out=`` writes each window's rows at their original positions (the VDN adapter's
+    ``out[plan.rows] = result``, ``integrations/vdn.py:64-70``), bit-identical to the gathered
+    result, and leaves every other row untouched."""
+    cpu, rows, keys = indexed_cases()
+    p = IndexedPlan.create(rows, keys, 1200, protected_ranges=((0, 7), (1180, 1193)), local_tokens=64)
+    gpu = [to_device(x) for x in cpu]
+    pd = p.to("cuda")
+    want, stats = sol_attention_indexed(*gpu, pd, beta=1.0, return_stats=True)
+    out = torch.full(gpu[0].shape, 7.0, dtype=torch.bfloat16, device="cuda")
+    got, stats2 = sol_attention_indexed(*gpu, pd, beta=1.0, return_stats=True, out=out)
+    assert got is out
+    r = rows.to("cuda")
+    assert torch.equal(out[r], want)
+    untouched = torch.ones(1200, dtype=torch.bool, device="cuda")
+    untouched[r.flatten()] = False
+    assert bool((out[untouched] == 7.0).all())
+    assert torch.equal(stats.exact_blocks, stats2.exact_blocks)
+
+
+def test_dense_attention_rows_matches_sdpa_and_gathered_dense():
+    """``dense_attention_rows`` (the adapter's dense step for global query rows) against FP32
+    SDPA of the gathered rows over all keys, and bit-identical to ``dense_attention`` of the
+    gathered rows; rows it does not name stay untouched."""
+    from sol_attn_b200 import dense_attention, dense_attention_rows
+    g = torch.Generator().manual_seed(5)
+    N, H, D = 1000, 3, 128
+    q, k, v = (torch.randn((N, H, D), generator=g, dtype=torch.bfloat16).cuda() for _ in range(3))
+    rows = torch.cat((torch.arange(0, 40), torch.arange(517, 600, 3), torch.tensor([999]))).cuda()
+    out = torch.full((N, H, D), -5.0, dtype=torch.bfloat16, device="cuda")
+    assert dense_attention_rows(q, k, v, rows, out=out) is out
+    ref = F.scaled_dot_product_attention(q[rows].float().transpose(0, 1)[None],
+                                         k.float().transpose(0, 1)[None],
+                                         v.float().transpose(0, 1)[None])[0].transpose(0, 1)
+    torch.testing.assert_close(out[rows].float(), ref, atol=0.012, rtol=0.025)
+    gathered = dense_attention(q[rows][None].contiguous(), k[None], v[None])[0]
+    assert torch.equal(out[rows], gathered)
+    untouched = torch.ones(N, dtype=torch.bool, device="cuda")
+    untouched[rows] = False
+    assert bool((out[untouched] == -5.0).all())
+    fresh = dense_attention_rows(q, k, v, rows)
+    assert torch.equal(fresh[rows], out[rows])

@@ -76,3 +76,21 @@ def test_forward_rejects_bad_arguments(bad, code):
 def test_threshold_rejects_nonfinite_beta():
     L = _lib.load()
     assert L.solattn_threshold(16, 16, 1, 1, 1, 1, 64, 0.125, float("inf"), 16, 16, 16, None) == -1
+
+
+def test_scatter_and_dense_rows_reject_bad_arguments():
+    """The scatter forward needs the query index and a positive row count; the dense-rows form
+    needs a row index, at least one row and a nonempty sequence (all rejected before any CUDA
+    call)."""
+    L = _lib.load()
+    st = (4096, 64, 64)
+    common = [16, 16, 16, 1, 64, 64, 1, 64, *st, *st, *st]
+    tail = [None, 0.125, 1.0, 1, 0, 0, 256, 1 << 20, 16]
+    assert L.solattn_sol_forward_scatter(*common, None, None, 0, *tail, 64, None, None) == -1
+    assert L.solattn_sol_forward_scatter(*common, 16, None, 64, *tail, 0, None, None) == -1
+    assert L.solattn_dense_rows(16, 16, 16, None, 4, 64, 1, 64, 64, 64, 64, 64, 64, 64, 0.125,
+                                16, None) == -1
+    assert L.solattn_dense_rows(16, 16, 16, 16, 0, 64, 1, 64, 64, 64, 64, 64, 64, 64, 0.125,
+                                16, None) == -1
+    assert L.solattn_dense_rows(16, 16, 16, 16, 4, 64, 1, 96, 64, 64, 64, 64, 64, 64, 0.125,
+                                16, None) == -2
