@@ -67,3 +67,18 @@ def test_scatter_and_dense_rows_reject_bad_arguments_on_cpu():
     plan = IndexedPlan.create(torch.arange(64)[None], torch.arange(64)[None], 100)
     with pytest.raises(ValueError, match="B200"):
         sol_attention_indexed(q, q, q, plan, out=torch.zeros_like(q))
+
+
+def test_bench_receipt_rejects_bad_runs_before_touching_the_gpu(tmp_path):
+    """The receipt keeps the reference's guards (``bench_attention.py:61-66``): finite beta,
+    positive counts, and a fresh output path (receipts are never overwritten)."""
+    from sol_attn_b200 import bench_receipt
+    out = tmp_path / "r.json"
+    with pytest.raises(SystemExit):
+        bench_receipt.main(["--beta", "inf", "--out", str(out)])
+    with pytest.raises(SystemExit):
+        bench_receipt.main(["--tokens", "0", "--out", str(out)])
+    out.write_text("{}")
+    with pytest.raises(SystemExit):
+        bench_receipt.main(["--out", str(out)])
+    assert out.read_text() == "{}"
