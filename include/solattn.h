@@ -170,6 +170,27 @@ SOLATTN_API int solattn_sol_forward_scatter(const void* q, const void* k, const 
                         void* out, int64_t out_rows, int32_t* counts, void* stream);
 
 /*
+ * solattn_sol_forward with both indexed extensions.  key_counts (device int32 [B], or NULL)
+ * gives window b its own number of keys, key_counts[b] in [1, Tk]: kv_idx rows are padded to
+ * Tk and only the first key_counts[b] of row b are read - one launch for windows whose key
+ * sets differ in size (a ragged IndexedPlan), with results identical to separate calls per
+ * window.  A count outside [1, Tk] is clamped and reported through the status word.
+ * key_counts requires kv_idx.  out_rows > 0 scatters into an NHD output exactly as
+ * solattn_sol_forward_scatter (requires q_idx); out_rows == 0 writes [B, Tq, H, D].
+ */
+SOLATTN_API int solattn_sol_forward_ex(const void* q, const void* k, const void* v,
+                        int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
+                        int64_t q_sB, int64_t q_sT, int64_t q_sH,
+                        int64_t k_sB, int64_t k_sT, int64_t k_sH,
+                        int64_t v_sB, int64_t v_sT, int64_t v_sH,
+                        const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
+                        const uint8_t* protect,
+                        float scale, float beta, int local, int kv_sink_blocks,
+                        int q_sink_blocks, void* workspace, int64_t workspace_bytes,
+                        const int32_t* key_counts, void* out, int64_t out_rows,
+                        int32_t* counts, void* stream);
+
+/*
  * Dense attention of a subset of query rows against all keys, written in place: for each
  * i < n_rows, out[rows[i]] = softmax(q[rows[i]] . k^T * scale) . v over all N keys, with q, k,
  * v and out NHD [N, H, D] BF16 (element strides q_sT/q_sH etc.; the head dimension is

@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int q0 = qb * kBlock;
+  // The batch's keys: its own count in a ragged launch (rows past it are never read).
+  const int tk = key_count(p, b), nkb_b = (tk + kBlock - 1) / kBlock;
 
   // ---- Q tile (cp.async, zero-fill past Tq) ----
   {
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
   const __nv_bfloat16* kc_bh = p.kc + (int64_t)bh * p.nkb * D;
   for (int w = warp; w < nwords; w += 4) {
     const int kb = 32 * w + lane;
-    const bool sel = kb < p.nkb && route_selected(p, sQbar, kc_bh + (int64_t)kb * D, cut, D, b, qb, kb);
+    const bool sel = kb < nkb_b && route_selected(p, sQbar, kc_bh + (int64_t)kb * D, cut, D, b, qb, kb);
     const uint32_t bal = __ballot_sync(0xffffffffu, sel);
     if (lane == 0) {
       sMask[w] = bal;
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
   // ---- tile list (warp 0) ----
   if (warp == 0) {
     int base = 0;
-    const int nct = (p.nkb + 63) / 64;
+    const int nct = (nkb_b + 63) / 64;
     if (p.force != 1) {
       for (int t0 = 0; t0 < nct; t0 += 32) {
         const int t = t0 + lane;
@@ -101,7 +103,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
         if (t < nct) {
           const uint32_t w0 = sMask[2 * t];
           const uint32_t w1 = (2 * t + 1 < nwords) ? sMask[2 * t + 1] : 0xffffffffu;
-          want = ((~w0 & valid_bits(2 * t, p.nkb)) | (~w1 & valid_bits(2 * t + 1, p.nkb))) != 0u;
+          want = ((~w0 & valid_bits(2 * t, nkb_b)) | (~w1 & valid_bits(2 * t + 1, nkb_b))) != 0u;
         }
         const uint32_t bal = __ballot_sync(0xffffffffu, want);
         if (want) sTiles[base + __popc(bal & ((1u << lane) - 1u))] = -(t + 1);
@@ -146,17 +148,17 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
     if (e >= 0) {
       const int t0 = e * kBlock;
       for (int r = tid / kChunks; r < kBlock; r += 128 / kChunks) {
-        const bool ok = t0 + r < p.Tk;
+        const bool ok = t0 + r < tk;
         const __nv_bfloat16* ks = ok ? row_ptr(p.k, p.Tk, b, h, t0 + r, p.status) : p.k.ptr;
         const __nv_bfloat16* vs = ok ? row_ptr(p.v, p.Tk, b, h, t0 + r, p.status) : p.v.ptr;
         cp_async16(swz<D>(kbase, r, chunk), ks + (ok ? chunk * 8 : 0), ok ? 16 : 0);
         cp_async16(swz<D>(vbase, r, chunk), vs + (ok ? chunk * 8 : 0), ok ? 16 : 0);
       }
-      if (tid < kBlock) sBias[buf * kBlock + tid] = (t0 + tid < p.Tk) ? 0.f : -INFINITY;
+      if (tid < kBlock) sBias[buf * kBlock + tid] = (t0 + tid < tk) ? 0.f : -INFINITY;
     } else {
       const int c0 = (-e - 1) * kBlock;
       for (int r = tid / kChunks; r < kBlock; r += 128 / kChunks) {
-        const bool ok = c0 + r < p.nkb;
+        const bool ok = c0 + r < nkb_b;
         const __nv_bfloat16* ks = ok ? kc_bh + (int64_t)(c0 + r) * D + chunk * 8 : p.kc;
         const __nv_bfloat16* vs = ok ? vc_bh + (int64_t)(c0 + r) * D + chunk * 8 : p.vc;
         cp_async16(swz<D>(kbase, r, chunk), ks, ok ? 16 : 0);
@@ -165,8 +167,8 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
       if (tid < kBlock) {
         const int c = c0 + tid;
         float bias = -INFINITY;
-        if (c < p.nkb && !((sMask[c >> 5] >> (c & 31)) & 1u)) {
-          const int len = min(kBlock, p.Tk - c * kBlock);
+        if (c < nkb_b && !((sMask[c >> 5] >> (c & 31)) & 1u)) {
+          const int len = min(kBlock, tk - c * kBlock);
           bias = log2f((float)len);
         }
         sBias[buf * kBlock + tid] = bias;

@@ -66,6 +66,12 @@ constexpr uint32_t kTmemO = 0, kTmemS = 256;  // O_x at kTmemO + 128 x
 constexpr int kQBox = kRows * 128;   // one 128-row x 64-column BF16 box of Q (16 KB)
 constexpr int kKVBox = kKeys * 128;  // one 64-row x 64-column BF16 box of K or V (8 KB)
 constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
+// Tile-list entry that pads an item to an even tile count, so that every item starts at an even
+// position of the CTA's tile sequence and its tiles split between the two softmax groups by
+// their item-local parity: the result of an item then does not depend on which CTA ran it
+// after which other items (bitwise repeatable under the dynamic schedule).  No keys, no loads,
+// no MMAs, P = 0.  Centroid entries are -(t + 1) >= -64.
+constexpr int kDummyTile = -32768;
 // Readers of an item's tile list that must be done before the producer overwrites it two items
 // later: the softmax warps, the two S issuers and the P V issuer.
 constexpr int kListReaders = kSoftmaxWarps + 3;
@@ -88,12 +94,13 @@ struct Layout {
   static constexpr int kK = 2 * kQTile;
   static constexpr int kV = kK + kStages * kKVTile;
   static constexpr int kBars = kV + kStages * kKVTile;
-  // uint32 [0] TMEM address [1] abort flag [2 + j] tiles, [4 + j] item of list buffer j
+  // uint32 [0] TMEM address [1] abort flag; of list buffer j: [2 + j] tiles (even), [4 + j]
+  // item, [6 + j] tiles with keys (the rest is one padding tile)
   static constexpr int kMisc = kBars + NBARS * 8;
   static constexpr int kMerge = kMisc + 32;  // float [2 items][8 warps][2][32 lanes]: m, l
   static constexpr int kMask = kMerge + 2 * 8 * 2 * 32 * 4;  // uint32 [2 items][2 q-blocks][nwords]
   __host__ __device__ static int tiles_offset(int nwords) { return kMask + 4 * nwords * 4; }
-  __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + nkb; }
+  __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + nkb + 1; }
   static size_t bytes(int nkb) {  // int16 tile lists [2 items][max_tiles]
     const int nwords = (nkb + 31) / 32;
     return 1024 + (size_t)tiles_offset(nwords) + 2 * (size_t)max_tiles(nkb) * 2;
@@ -134,6 +141,10 @@ template <int D>
 __device__ __forceinline__ void load_kv_tile(uint32_t dst, const CUtensorMap* tile_map,
                                              const CUtensorMap* cent_map, uint32_t full, int e,
                                              int h, int b) {
+  if (e == kDummyTile) {  // a padding tile loads nothing
+    mbar_arrive(full);
+    return;
+  }
   mbar_expect_tx(full, (uint32_t)(kKeys * D * 2));
   const bool cent = e < 0;
   const int row = cent ? kKeys * (-e - 1) : kBlock * e;
@@ -268,6 +279,7 @@ __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPo
                                                const MaskWords& mw, uint32_t* m, int16_t* tiles,
                                                int nwords, int lane) {
   const bool has1 = ip.qb0 + 1 < p.nqb;
+  const int nkb_b = (key_count(p, ip.b) + kBlock - 1) / kBlock;  // this batch's key blocks
   if (p.masks) {
 #pragma unroll
     for (int j = 0; j < kMaskRegs; ++j)
@@ -275,7 +287,7 @@ __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPo
   } else {
     for (int i = 0; i < 2 * nwords; ++i) {
       const int qb = ip.qb0 + i / nwords, kb = 32 * (i % nwords) + lane;
-      const bool sel = qb < p.nqb && kb < p.nkb && route_rules(p, false, ip.b, qb, kb);
+      const bool sel = qb < p.nqb && kb < nkb_b && route_rules(p, false, ip.b, qb, kb);
       const uint32_t bal = __ballot_sync(0xffffffffu, sel);
       if (lane == 0) m[i] = bal;
     }
@@ -284,13 +296,13 @@ __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPo
   const uint32_t* m0 = m;
   const uint32_t* m1 = m + nwords;
   int n = 0;
-  const int nct = p.force == 1 ? 0 : (p.nkb + kKeys - 1) / kKeys;
+  const int nct = p.force == 1 ? 0 : (nkb_b + kKeys - 1) / kKeys;
   for (int t0 = 0; t0 < nct; t0 += 32) {
     const int t = t0 + lane;
     bool useful = false;
     if (t < nct) {
       for (int wi = 2 * t; wi < 2 * t + 2 && wi < nwords; ++wi) {
-        const uint32_t v = valid_word(wi, p.nkb);
+        const uint32_t v = valid_word(wi, nkb_b);
         if ((~m0[wi] & v) || (has1 && (~m1[wi] & v))) useful = true;
       }
     }
@@ -323,8 +335,13 @@ __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPo
     for (int i = 0; i < nwords; ++i) c += __popc(m[lane * nwords + i]);
     p.counts[((int64_t)ip.b * p.nqb + ip.qb0 + lane) * p.H + ip.h] = c;
   }
+  n += r;
+  if (n & 1) {  // even tile counts: every item starts at an even tile position
+    if (lane == 0) tiles[n] = (int16_t)kDummyTile;
+    ++n;
+  }
   __syncwarp();
-  return n + r;
+  return n;
 }
 
 // Item epilogue of one softmax warp: wait for the group's last P V, exchange the running max
@@ -548,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         misc[2 + lb] = (uint32_t)ntiles;
         misc[4 + lb] = (uint32_t)item;
+        misc[6 + lb] = (uint32_t)(ntiles - (tl[ntiles - 1] == kDummyTile ? 1 : 0));
         mbar_arrive(bar(LIST_FULL + lb));
       }
       mw = load_mask_words(p, next, total, nwords, lane);
@@ -580,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto row_idx = [&](int e) {
           RowIdx<kKeys> ri;
           if (e >= 0) {
-            ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, p.Tk - e * kBlock, lane,
+            ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, key_count(p, ip.b) - e * kBlock, lane,
                                      p.status);
           } else {
             ri.t[0] = ri.t[1] = 0;
@@ -597,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (e >= 0) gather_tile<D, kKeys>(sK + s * L::kKVTile, kKVBox, p.k, ri, ip.h, lane, bar(K_FULL + s));
-          else if (lane == 0) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, ip.h, ip.b);
+          else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, ip.h, ip.b);
           else mbar_arrive(bar(K_FULL + s));
           ++k_issued;
           if (gi >= kStages && !warp_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
@@ -605,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (e >= 0) gather_tile<D, kKeys>(sV + s * L::kKVTile, kKVBox, p.v, ri, ip.h, lane, bar(V_FULL + s));
-          else if (lane == 0) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, ip.h, ip.b);
+          else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, ip.h, ip.b);
           else mbar_arrive(bar(V_FULL + s));
           ++v_issued;
           if (i + 1 < ntiles) ri = row_idx(tl[i + 1]);
@@ -641,6 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!warp_wait(bar(LIST_FULL + lb), (uint32_t)(k >> 1) & 1u, abort_flag, p.status)) break;
       const int item = (int)vmisc[4 + lb];
       const int ntiles = (int)vmisc[2 + lb];
+      const int real = (int)vmisc[6 + lb];  // tiles with keys; the rest is a padding tile
       if (item < 0) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(LIST_EMPTY + lb));
@@ -657,15 +676,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (p.k.idx) fence_proxy_async_smem();  // gathered V rows were written by cp.async
         if (lane == 0) {
-          const uint64_t vd = dV + (uint64_t)s * kSlotStep;
-          const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
-          const uint32_t tO = tmem + kTmemO + (uint32_t)(128 * (gi & 1));  // the tile's group
-          // Local tiles 0 and 1 are each group's first of the item: they start the accumulator.
+          if (i < real) {
+            const uint64_t vd = dV + (uint64_t)s * kSlotStep;
+            const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
+            const uint32_t tO = tmem + kTmemO + (uint32_t)(128 * (gi & 1));  // the tile's group
+            // Local tiles 0 and 1 are each group's first of the item (items start at even
+            // tile positions): they start the accumulator.
 #pragma unroll
-          for (int kk = 0; kk < kKeys / 16; ++kk)
-            mma_ts(tO, tP + (uint32_t)(8 * kk), vd + (uint64_t)((kk * 16 * 128) >> 4), idO,
-                   (i > 1 || kk > 0) ? 1u : 0u);
-          mma_commit(bar(PV_DONE + s));
+            for (int kk = 0; kk < kKeys / 16; ++kk)
+              mma_ts(tO, tP + (uint32_t)(8 * kk), vd + (uint64_t)((kk * 16 * 128) >> 4), idO,
+                     (i > 1 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar(PV_DONE + s));  // a padding tile: once the MMAs before it completed
         }
         __syncwarp();
       }
@@ -690,6 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!warp_wait(bar(LIST_FULL + lb), iph, abort_flag, p.status)) break;
       const int item = (int)vmisc[4 + lb];
       const int ntiles = (int)vmisc[2 + lb];
+      const int real = (int)vmisc[6 + lb];  // tiles with keys; the rest is a padding tile
       if (item < 0) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(LIST_EMPTY + lb));
@@ -714,14 +737,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (p.k.idx) fence_proxy_async_smem();  // gathered K rows were written by cp.async
         if (lane == 0) {
-          const uint64_t kd = dK + (uint64_t)s * kSlotStep;
-          const uint32_t tS = tmem + kTmemS + (uint32_t)(kKeys * s);
+          if (i < real) {
+            const uint64_t kd = dK + (uint64_t)s * kSlotStep;
+            const uint32_t tS = tmem + kTmemS + (uint32_t)(kKeys * s);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t off = (uint64_t)(((kk >> 2) * kQBox + (kk & 3) * 32) >> 4);
-            const uint64_t offk = (uint64_t)(((kk >> 2) * kKVBox + (kk & 3) * 32) >> 4);
-            mma_ss(tS, dQ + off, kd + offk, idS, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t off = (uint64_t)(((kk >> 2) * kQBox + (kk & 3) * 32) >> 4);
+              const uint64_t offk = (uint64_t)(((kk >> 2) * kKVBox + (kk & 3) * 32) >> 4);
+              mma_ss(tS, dQ + off, kd + offk, idS, kk > 0 ? 1u : 0u);
+            }
           }
+          // (a padding tile: both barriers once the MMAs before it completed)
           mma_commit(bar(S_FULL + s));
           mma_commit(bar(K_EMPTY + s));
         }
@@ -746,10 +772,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
     const uint64_t six2 = f2_pack(6.f, 6.f);  // log2(64): bias of a full block's centroid
-    const int last_len = p.Tk - (p.nkb - 1) * kBlock;
-    const float last_bias = log2f((float)last_len);
-    const int last_col = (p.nkb - 1) & 63;  // column of the last centroid in its group
-    const int last_group = (p.nkb - 1) >> 6;
     int g = 0;
     bool ok = true;
     for (int k = 0; ok; ++k) {
@@ -758,8 +780,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int item = (int)vmisc[4 + lb];
       if (item < 0) break;
       const int ntiles = (int)vmisc[2 + lb];
+      const ItemPos ip = item_pos(p, item);
       // The warp's q-block exists (only the last pair of a head can lack its second q-block).
-      const bool warp_rows = qsel == 0 || item_pos(p, item).qb0 + 1 < p.nqb;
+      const bool warp_rows = qsel == 0 || ip.qb0 + 1 < p.nqb;
+      // The batch's keys (its own count in a ragged launch) and its last, maybe partial, block.
+      const int tk = key_count(p, ip.b), nkb_b = (tk + kBlock - 1) / kBlock;
+      const int last_len = tk - (nkb_b - 1) * kBlock;
+      const float last_bias = log2f((float)last_len);
+      const int last_col = (nkb_b - 1) & 63;  // column of the last centroid in its group
+      const int last_group = (nkb_b - 1) >> 6;
       const uint32_t* mymask = sMask + (lb * 2 + qsel) * nwords;
       const int16_t* tl = sTiles + lb * max_tiles;
       float m_run = -INFINITY, l_run = 0.f;
@@ -769,17 +798,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Tile metadata first: these shared-memory reads overlap the wait for S.  Every value
         // below is warp-uniform (one q-block per warp).
         const int entry = tl[i];
-        const bool centroid = entry < 0;
+        const bool dummy = entry == kDummyTile;
+        const bool centroid = entry < 0 && !dummy;
         uint32_t approx0 = 0u, approx1 = 0u;  // centroid columns this q-block uses
         int len = 0;                          // valid keys of an exact block it selected
         if (centroid) {
           const int t = -entry - 1;  // 2t < nwords since t <= (nkb - 1) / 64
           if (warp_rows) {
-            approx0 = ~mymask[2 * t] & valid_word(2 * t, p.nkb);
-            if (2 * t + 1 < nwords) approx1 = ~mymask[2 * t + 1] & valid_word(2 * t + 1, p.nkb);
+            approx0 = ~mymask[2 * t] & valid_word(2 * t, nkb_b);
+            if (2 * t + 1 < nwords) approx1 = ~mymask[2 * t + 1] & valid_word(2 * t + 1, nkb_b);
           }
-        } else if (warp_rows && ((mymask[entry >> 5] >> (entry & 31)) & 1u)) {
-          len = min(kBlock, p.Tk - entry * kBlock);
+        } else if (!dummy && warp_rows && ((mymask[entry >> 5] >> (entry & 31)) & 1u)) {
+          len = min(kBlock, tk - entry * kBlock);
         }
         const bool active = centroid ? (approx0 | approx1) != 0u : len > 0;
         if (!warp_wait(bar(S_FULL + s), (uint32_t)(gi / kStages) & 1u, abort_flag, p.status)) {
@@ -930,7 +960,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // ---- item epilogue ----
-      if (!item_epilogue<D>(tmem, bar0, warp, lane, k, last, m_run, l_run, ntiles, g,
+      // Tiles with keys decide which accumulators hold this item.
+      if (!item_epilogue<D>(tmem, bar0, warp, lane, k, last, m_run, l_run, (int)vmisc[6 + lb], g,
                             (int)vmisc[4 + lb], sMerge, abort_flag, p.status, p.out, p.out_idx,
                             p.out_rows, p.Tq, p.H, p.nqb, p.q_sink_blocks, p.B))
         break;
@@ -998,7 +1029,8 @@ bool make_pooled_map(CUtensorMap* map, const __nv_bfloat16* base, int B, int H, 
 
 template <int D>
 cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
-  if (p.nkb > kMaxKeyBlocks || (p.masks == nullptr && p.force == 0)) return cudaErrorInvalidValue;
+  if (p.nkb > kMaxKeyBlocks || (p.masks == nullptr && p.force == 0) || (p.tk_b && !p.k.idx))
+    return cudaErrorInvalidValue;
   // Gathered (indexed) inputs are copied by the producer warp and need no tensor map.
   CUtensorMap tmQ, tmK, tmV, tmKC, tmVC;
   memset(&tmQ, 0, sizeof(tmQ));

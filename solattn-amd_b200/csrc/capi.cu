@@ -11,7 +11,7 @@ namespace solattn {
 cudaError_t launch_pool(const PoolParams& p, int D, cudaStream_t stream);
 cudaError_t launch_threshold(const __nv_bfloat16* kc, const float* qc, int BH, int H, int nqb,
                              int nkb, int D, float scale, float beta, float* mean, float* var,
-                             float* cutoff, cudaStream_t stream);
+                             float* cutoff, const int32_t* tk_b, cudaStream_t stream);
 cudaError_t launch_attention(const AttnParams& p, int D, cudaStream_t stream);
 }  // namespace solattn
 
@@ -83,6 +83,12 @@ Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   return L;
 }
 
+int pool_impl(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,
+              int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH, int64_t k_sB,
+              int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT, int64_t v_sH,
+              const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows, int pool_q, float* qc,
+              void* kc, void* vc, const int32_t* key_counts, int32_t* status, void* stream);
+
 // Rows of the underlying tensor addressed by a gather index (bounds for the device check).
 int64_t gather_rows(const int64_t* idx, int64_t idx_rows, int64_t T) { return idx ? idx_rows : T; }
 
@@ -127,6 +133,31 @@ int solattn_pool_qkv(const void* q, const void* k, const void* v, int64_t B, int
                      int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT,
                      int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
                      int pool_q, float* qc, void* kc, void* vc, int32_t* status, void* stream) {
+  return pool_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT, v_sH,
+                   q_idx, kv_idx, idx_rows, pool_q, qc, kc, vc, nullptr, status, stream);
+}
+
+int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int64_t nqb,
+                      int64_t nkb, int64_t D, float scale, float beta, float* mean, float* var,
+                      float* cutoff, void* stream) {
+  if (B <= 0 || H <= 0 || nqb <= 0 || nkb <= 0 || nkb > kMaxBlocks) return SOLATTN_ERR_ARG;
+  if (D != 64 && D != 128) return SOLATTN_ERR_UNSUPPORTED;
+  if (!kc || !qc || !mean || !var || !cutoff) return SOLATTN_ERR_ARG;
+  if (!(scale > 0.f) || !isfinite(scale) || !isfinite(beta)) return SOLATTN_ERR_ARG;
+  return from_cuda(launch_threshold(static_cast<const __nv_bfloat16*>(kc), qc, (int)(B * H),
+                                    (int)H, (int)nqb, (int)nkb, (int)D, scale, beta, mean, var,
+                                    cutoff, nullptr, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"
+
+namespace {
+
+int pool_impl(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,
+              int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH, int64_t k_sB,
+              int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT, int64_t v_sH,
+              const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows, int pool_q, float* qc,
+              void* kc, void* vc, const int32_t* key_counts, int32_t* status, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (!k || !v || !kc || !vc || (pool_q && (!q || !qc))) return SOLATTN_ERR_ARG;
@@ -150,25 +181,10 @@ int solattn_pool_qkv(const void* q, const void* k, const void* v, int64_t B, int
   p.y[2] = vc;
   p.B = (int)B;
   p.H = (int)H;
+  p.tk_b = key_counts;
   p.status = status;
   return from_cuda(launch_pool(p, (int)D, static_cast<cudaStream_t>(stream)));
 }
-
-int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int64_t nqb,
-                      int64_t nkb, int64_t D, float scale, float beta, float* mean, float* var,
-                      float* cutoff, void* stream) {
-  if (B <= 0 || H <= 0 || nqb <= 0 || nkb <= 0 || nkb > kMaxBlocks) return SOLATTN_ERR_ARG;
-  if (D != 64 && D != 128) return SOLATTN_ERR_UNSUPPORTED;
-  if (!kc || !qc || !mean || !var || !cutoff) return SOLATTN_ERR_ARG;
-  if (!(scale > 0.f) || !isfinite(scale) || !isfinite(beta)) return SOLATTN_ERR_ARG;
-  return from_cuda(launch_threshold(static_cast<const __nv_bfloat16*>(kc), qc, (int)(B * H),
-                                    (int)H, (int)nqb, (int)nkb, (int)D, scale, beta, mean, var,
-                                    cutoff, static_cast<cudaStream_t>(stream)));
-}
-
-}  // extern "C"
-
-namespace {
 
 // solattn_attention with an optional output row index (out_idx [B, Tq], out_rows rows of an NHD
 // output); see solattn_sol_forward_scatter.
@@ -179,13 +195,14 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
                    const void* kc, const void* vc, const float* qc, const float* cutoff,
                    const uint8_t* protect, float scale, int force, int local,
                    int kv_sink_blocks, int q_sink_blocks, void* out, const int64_t* out_idx,
-                   int64_t out_rows, int32_t* counts, int32_t* status, uint32_t* masks,
-                   void* stream) {
+                   int64_t out_rows, const int32_t* key_counts, int32_t* counts, int32_t* status,
+                   uint32_t* masks, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (!q || !k || !v || !kc || !vc || !out) return SOLATTN_ERR_ARG;
   if (force == SOLATTN_FORCE_THRESHOLD && !masks) return SOLATTN_ERR_ARG;
   if (out_idx && out_rows <= 0) return SOLATTN_ERR_ARG;
+  if (key_counts && !kv_idx) return SOLATTN_ERR_ARG;  // ragged key counts: indexed inputs only
   if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
   if (force < 0 || force > 2 || (force == 0 && (!qc || !cutoff))) return SOLATTN_ERR_ARG;
   if (!(scale > 0.f) || !isfinite(scale) || kv_sink_blocks < 0 || q_sink_blocks < 0)
@@ -217,6 +234,7 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
   p.H = (int)H;
   p.nqb = (int)cdiv(Tq, kBlock);
   p.nkb = (int)cdiv(Tk, kBlock);
+  p.tk_b = key_counts;
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.force = force;
@@ -233,7 +251,7 @@ int sol_forward_impl(const void* q, const void* k, const void* v, int64_t B, int
                      const uint8_t* protect, float scale, float beta, int local,
                      int kv_sink_blocks, int q_sink_blocks, void* workspace,
                      int64_t workspace_bytes, void* out, const int64_t* out_idx, int64_t out_rows,
-                     int32_t* counts, void* stream) {
+                     const int32_t* key_counts, int32_t* counts, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (isnan(beta) || !workspace) return SOLATTN_ERR_ARG;
@@ -244,6 +262,7 @@ int sol_forward_impl(const void* q, const void* k, const void* v, int64_t B, int
       !strides_ok(v_sB, v_sT, v_sH))
     return SOLATTN_ERR_ARG;
   if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
+  if (key_counts && !kv_idx) return SOLATTN_ERR_ARG;
   if (!(scale > 0.f) || !isfinite(scale) || kv_sink_blocks < 0 || q_sink_blocks < 0)
     return SOLATTN_ERR_ARG;
   const Layout L = layout(B, Tq, Tk, H, D);
@@ -261,22 +280,24 @@ int sol_forward_impl(const void* q, const void* k, const void* v, int64_t B, int
   if (cudaMemsetAsync(status, 0, sizeof(int32_t), static_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
     return SOLATTN_ERR_CUDA;
-  rc = solattn_pool_qkv(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT,
-                        v_sH, q_idx, kv_idx, idx_rows, force == SOLATTN_FORCE_THRESHOLD, qc, kc, vc,
-                        status, stream);
+  rc = pool_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT, v_sH,
+                 q_idx, kv_idx, idx_rows, force == SOLATTN_FORCE_THRESHOLD, qc, kc, vc, key_counts,
+                 status, stream);
   if (rc) return rc;
   if (force == SOLATTN_FORCE_THRESHOLD) {
-    rc = solattn_threshold(kc, qc, B, H, nqb, nkb, D, scale, beta,
-                           reinterpret_cast<float*>(ws + L.mean),
-                           reinterpret_cast<float*>(ws + L.var), cutoff, stream);
+    rc = from_cuda(launch_threshold(static_cast<const __nv_bfloat16*>(kc), qc, (int)(B * H),
+                                    (int)H, (int)nqb, (int)nkb, (int)D, scale, beta,
+                                    reinterpret_cast<float*>(ws + L.mean),
+                                    reinterpret_cast<float*>(ws + L.var), cutoff, key_counts,
+                                    static_cast<cudaStream_t>(stream)));
     if (rc) return rc;
   }
   return attention_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
                         v_sT, v_sH, q_idx, kv_idx, idx_rows, kc, vc,
                         force == SOLATTN_FORCE_THRESHOLD ? qc : nullptr,
                         force == SOLATTN_FORCE_THRESHOLD ? cutoff : nullptr, protect, scale, force,
-                        local, kv_sink_blocks, q_sink_blocks, out, out_idx, out_rows, counts,
-                        status, reinterpret_cast<uint32_t*>(ws + L.masks), stream);
+                        local, kv_sink_blocks, q_sink_blocks, out, out_idx, out_rows, key_counts,
+                        counts, status, reinterpret_cast<uint32_t*>(ws + L.masks), stream);
 }
 
 }  // namespace
@@ -293,8 +314,8 @@ int solattn_attention(const void* q, const void* k, const void* v, int64_t B, in
                       int32_t* status, uint32_t* masks, void* stream) {
   return attention_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT,
                         v_sH, q_idx, kv_idx, idx_rows, kc, vc, qc, cutoff, protect, scale, force,
-                        local, kv_sink_blocks, q_sink_blocks, out, nullptr, 0, counts, status,
-                        masks, stream);
+                        local, kv_sink_blocks, q_sink_blocks, out, nullptr, 0, nullptr, counts,
+                        status, masks, stream);
 }
 
 int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
@@ -307,7 +328,7 @@ int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, 
   return sol_forward_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
                           v_sT, v_sH, q_idx, kv_idx, idx_rows, protect, scale, beta, local,
                           kv_sink_blocks, q_sink_blocks, workspace, workspace_bytes, out, nullptr,
-                          0, counts, stream);
+                          0, nullptr, counts, stream);
 }
 
 int solattn_sol_forward_scatter(const void* q, const void* k, const void* v, int64_t B,
@@ -323,7 +344,22 @@ int solattn_sol_forward_scatter(const void* q, const void* k, const void* v, int
   return sol_forward_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
                           v_sT, v_sH, q_idx, kv_idx, idx_rows, protect, scale, beta, local,
                           kv_sink_blocks, q_sink_blocks, workspace, workspace_bytes, out, q_idx,
-                          out_rows, counts, stream);
+                          out_rows, nullptr, counts, stream);
+}
+
+int solattn_sol_forward_ex(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
+                           int64_t Tk, int64_t H, int64_t D, int64_t q_sB, int64_t q_sT,
+                           int64_t q_sH, int64_t k_sB, int64_t k_sT, int64_t k_sH, int64_t v_sB,
+                           int64_t v_sT, int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx,
+                           int64_t idx_rows, const uint8_t* protect, float scale, float beta,
+                           int local, int kv_sink_blocks, int q_sink_blocks, void* workspace,
+                           int64_t workspace_bytes, const int32_t* key_counts, void* out,
+                           int64_t out_rows, int32_t* counts, void* stream) {
+  if (out_rows < 0 || (out_rows > 0 && !q_idx)) return SOLATTN_ERR_ARG;
+  return sol_forward_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
+                          v_sT, v_sH, q_idx, kv_idx, idx_rows, protect, scale, beta, local,
+                          kv_sink_blocks, q_sink_blocks, workspace, workspace_bytes, out,
+                          out_rows > 0 ? q_idx : nullptr, out_rows, key_counts, counts, stream);
 }
 
 int solattn_dense_rows(const void* q, const void* k, const void* v, const int64_t* rows,
@@ -336,7 +372,7 @@ int solattn_dense_rows(const void* q, const void* k, const void* v, const int64_
   return attention_impl(q, k, v, 1, n_rows, N, H, D, 0, q_sT, q_sH, 0, k_sT, k_sH, 0, v_sT, v_sH,
                         rows, nullptr, N, k, v, nullptr, nullptr, nullptr, scale,
                         SOLATTN_FORCE_ALL, -1, 0, 0, out, rows, N, nullptr, nullptr, nullptr,
-                        stream);
+                        nullptr, stream);
 }
 
 int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,

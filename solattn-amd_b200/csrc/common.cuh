@@ -40,6 +40,8 @@ struct AttnParams {
   uint32_t* masks;          // [B, H, nqb, ceil(nkb/32)] routing bitmask: written by route.cu
                             // (read by attn_sm100_kernel) or by attn_mma_kernel
   int B, Tq, Tk, H, nqb, nkb;
+  const int32_t* tk_b;  // optional per-batch key counts [B] (ragged indexed plans: batch b has
+                        // tk_b[b] <= Tk keys, ceil(tk_b[b] / 64) key blocks), else nullptr
   float scale;       // softmax scale (natural-log units), used by routing
   float scale_log2;  // scale * log2(e), used by the softmax
   int force, local, kv_sink_blocks, q_sink_blocks;
@@ -50,6 +52,7 @@ struct PoolParams {
   int T[3];          // Tq, Tk, Tk
   int nb[3];         // blocks per tensor
   int64_t units[3];  // units per tensor (B*nb*H); 0 skips the tensor
+  const int32_t* tk_b;  // optional per-batch key counts [B] for K and V (ragged), else nullptr
   void* y[3];        // qc (float), kc (bf16), vc (bf16)
   int B, H;
   int32_t* status;
@@ -181,6 +184,19 @@ __device__ __forceinline__ void routing_dot2(const float* qa, const float* qb,
                  __fadd_rn(__fadd_rn(pa[4], pa[5]), __fadd_rn(pa[6], pa[7])));
   db = __fadd_rn(__fadd_rn(__fadd_rn(pb[0], pb[1]), __fadd_rn(pb[2], pb[3])),
                  __fadd_rn(__fadd_rn(pb[4], pb[5]), __fadd_rn(pb[6], pb[7])));
+}
+
+// Keys of batch b: its own count in a ragged launch (a count outside [1, Tk] is reported and
+// clamped, so that every index derived from it stays in range), else Tk.
+__device__ __forceinline__ int clamp_key_count(int n, int Tk, int32_t* status) {
+  if (n < 1 || n > Tk) {
+    report(status, kStatusBadIndex);
+    n = n < 1 ? 1 : Tk;
+  }
+  return n;
+}
+__device__ __forceinline__ int key_count(const AttnParams& p, int b) {
+  return p.tk_b ? clamp_key_count(__ldg(p.tk_b + b), p.Tk, p.status) : p.Tk;
 }
 
 // The force modes and the local / sink / protected rules (reference.py:41-51,

@@ -5,7 +5,8 @@
 // g, g+8, ..., g+56 (all eight 128-bit loads issued before any add), accumulating in FP32.
 // The 8 group partials are combined through shared memory in group order, then divided by
 // the valid row count min(64, T - 64*block) with IEEE division.  K/V means are rounded to
-// BF16 (nearest even), Q means stay FP32.  Output layout is [B, H, blocks, D].
+// BF16 (nearest even), Q means stay FP32.  Output layout is [B, H, blocks, D].  In a ragged
+// launch batch b has its own key count (K/V blocks past it hold zeros).
 //
 // The pass is HBM-bound: it reads every Q/K/V element once (the 64 rows of a unit are
 // strided by sT, each row a contiguous 2*D-byte segment) and writes 1/64 of that back.
@@ -42,7 +43,9 @@ __global__ void __launch_bounds__(256) pool_kernel(PoolParams p) {
     int64_t r = unit / p.H;
     blk = (int)(r % p.nb[which]);
     b = (int)(r / p.nb[which]);
-    n = min(kBlock, T - blk * kBlock);
+    const int Tv = (which > 0 && p.tk_b) ? clamp_key_count(__ldg(p.tk_b + b), T, p.status)
+                                         : T;  // valid rows of this batch
+    n = min(kBlock, Tv - blk * kBlock);
     uint4 raw[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -74,7 +77,7 @@ __global__ void __launch_bounds__(256) pool_kernel(PoolParams p) {
   float s = 0.f;
 #pragma unroll
   for (int gg = 0; gg < 8; ++gg) s = __fadd_rn(s, part[local_unit][gg][lt]);
-  const float mean = __fdiv_rn(s, (float)n);
+  const float mean = n > 0 ? __fdiv_rn(s, (float)n) : 0.f;
   const int nb = p.nb[which];
   const int64_t o = (((int64_t)b * p.H + h) * nb + blk) * D + lt;
   if (which == 0) {

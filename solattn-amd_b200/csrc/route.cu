@@ -28,6 +28,7 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   const int qb_lo = blockIdx.x * kRouteQB;
   const int nq = min(kRouteQB, p.nqb - qb_lo);
   const int nwords = (p.nkb + 31) / 32;
+  const int nkb_b = (key_count(p, b) + kBlock - 1) / kBlock;  // this batch's key blocks
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
     p.masks[(int64_t)p.B * p.H * p.nqb * nwords] = 0u;
   for (int i = threadIdx.x; i < kRouteQB * D; i += kRouteThreads) {
@@ -64,7 +65,7 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
           const int idx = 32 * t + lane, r = idx >> 3, c = idx & 7;
-          const int kr = min(32 * w + r, p.nkb - 1);  // clamped: every address stays in range
+          const int kr = min(32 * w + r, nkb_b - 1);  // clamped: every address stays in range
           const uint4 v = __ldg(reinterpret_cast<const uint4*>(kc_bh + (int64_t)kr * D + 64 * half) + c);
           *reinterpret_cast<uint4*>(my_stage + r * kRowBytes + 16 * c) = v;
         }
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
                                   __fadd_rn(__fadd_rn(part[j][4], part[j][5]),
                                             __fadd_rn(part[j][6], part[j][7])));
       bool sel = false;
-      if (kb < p.nkb) sel = route_rules(p, p.force == 0 && __fmul_rn(dot, p.scale) > scut[j], b, qb, kb);
+      if (kb < nkb_b) sel = route_rules(p, p.force == 0 && __fmul_rn(dot, p.scale) > scut[j], b, qb, kb);
       const uint32_t bal = __ballot_sync(0xffffffffu, sel);
       if (lane == 0) p.masks[((int64_t)bh * p.nqb + qb) * nwords + w] = bal;
     }

@@ -20,7 +20,8 @@ constexpr int kThrQB = 32;  // q-blocks per CTA
 template <int D>
 __global__ void __launch_bounds__(D) threshold_kernel(const __nv_bfloat16* __restrict__ kc,
                                                       const float* __restrict__ qc, int nqb,
-                                                      int nkb, float scale, float beta,
+                                                      int nkb, const int32_t* __restrict__ tk_b,
+                                                      int H, float scale, float beta,
                                                       float* mean_out, float* var_out,
                                                       float* cutoff) {
   __shared__ float s_mean[D];
@@ -33,13 +34,15 @@ __global__ void __launch_bounds__(D) threshold_kernel(const __nv_bfloat16* __res
   for (int i = d; i < nq * D; i += D)
     s_q[i / D][i % D] = qc[((int64_t)bh * nqb + qb0) * D + i];
   const __nv_bfloat16* base = kc + (int64_t)bh * nkb * D + d;
+  // The batch's own key blocks in a ragged launch (kc rows past them are padding).
+  const int nb = tk_b ? min(max((tk_b[bh / H] + kBlock - 1) / kBlock, 1), nkb) : nkb;
   float s1 = 0.f, s2 = 0.f;
-  for (int j = 0; j < nkb; ++j) {
+  for (int j = 0; j < nb; ++j) {
     const float x = __bfloat162float(base[(int64_t)j * D]);
     s1 = __fadd_rn(s1, x);
     s2 = __fadd_rn(s2, __fmul_rn(x, x));
   }
-  const float n = (float)nkb;
+  const float n = (float)nb;
   const float mean = __fdiv_rn(s1, n);
   const float var = fmaxf(__fsub_rn(__fdiv_rn(s2, n), __fmul_rn(mean, mean)), 0.f);
   s_mean[d] = mean;
@@ -65,15 +68,14 @@ __global__ void __launch_bounds__(D) threshold_kernel(const __nv_bfloat16* __res
 
 cudaError_t launch_threshold(const __nv_bfloat16* kc, const float* qc, int BH, int H, int nqb,
                              int nkb, int D, float scale, float beta, float* mean, float* var,
-                             float* cutoff, cudaStream_t stream) {
-  (void)H;
+                             float* cutoff, const int32_t* tk_b, cudaStream_t stream) {
   const dim3 grid((nqb + kThrQB - 1) / kThrQB, BH);
   if (D == 128)
-    threshold_kernel<128><<<grid, 128, 0, stream>>>(kc, qc, nqb, nkb, scale, beta, mean, var,
-                                                    cutoff);
+    threshold_kernel<128><<<grid, 128, 0, stream>>>(kc, qc, nqb, nkb, tk_b, H, scale, beta, mean,
+                                                    var, cutoff);
   else
-    threshold_kernel<64><<<grid, 64, 0, stream>>>(kc, qc, nqb, nkb, scale, beta, mean, var,
-                                                  cutoff);
+    threshold_kernel<64><<<grid, 64, 0, stream>>>(kc, qc, nqb, nkb, tk_b, H, scale, beta, mean,
+                                                  var, cutoff);
   return cudaGetLastError();
 }
 

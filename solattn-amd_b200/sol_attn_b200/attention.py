@@ -27,9 +27,13 @@ class SolStats:
 
     # Device tensor [batch, query_blocks, heads]; obtaining a Python density syncs.
     exact_blocks: torch.Tensor
+    # Key blocks per query block; for a ragged indexed plan a per-window int tensor
+    # [batch, 1, 1] on the same device (windows have different key counts).
     key_blocks: int
 
     def density(self) -> float:
+        if isinstance(self.key_blocks, torch.Tensor):
+            return (self.exact_blocks.float() / self.key_blocks).mean().item()
         return self.exact_blocks.float().mean().item() / self.key_blocks
 
 
@@ -82,13 +86,14 @@ def _strides(x: torch.Tensor, indexed: bool):
 
 
 def launch_sol(q, k, v, scale, beta, local, kv_sink, q_sink, stats, protection=None,
-               rows=None, keys=None, out=None):
+               rows=None, keys=None, out=None, key_counts=None):
     """Allocate outputs + workspace and run the all-in forward (``kernels.py:203-225``).
 
     BTHD inputs, or NHD inputs with gather indices ``rows`` [W, nq] / ``keys`` [W, nk]
     (then the logical shape is B=W, Tq=nq, Tk=nk).  With ``out`` (indexed only: an NHD tensor
     like ``q``) each query row's output is written to ``out[rows[w, i]]`` instead of a fresh
-    [W, nq, H, D] tensor.  Returns (out, counts).
+    [W, nq, H, D] tensor.  ``key_counts`` (int32 [W] on the device) gives each window its own
+    key count in a ragged plan (``keys`` padded to the longest window).  Returns (out, counts).
     """
     indexed = rows is not None
     # The kernels need 16-byte-aligned rows; other positive strides are made contiguous first.
@@ -121,7 +126,12 @@ def launch_sol(q, k, v, scale, beta, local, kv_sink, q_sink, stats, protection=N
             protection.data_ptr() if protection is not None else None,
             float(scale), float(beta), int(local), (kv_sink + BLOCK - 1) // BLOCK,
             (q_sink + BLOCK - 1) // BLOCK, ws_ptr, total, out.data_ptr())
-    if scatter:
+    if key_counts is not None:
+        rc = L.solattn_sol_forward_ex(*args[:-1], key_counts.data_ptr(), out.data_ptr(),
+                                      out.shape[0] if scatter else 0,
+                                      counts.data_ptr() if stats else None, stream)
+        _lib.check(rc, "solattn_sol_forward_ex")
+    elif scatter:
         rc = L.solattn_sol_forward_scatter(*args, out.shape[0],
                                            counts.data_ptr() if stats else None, stream)
         _lib.check(rc, "solattn_sol_forward_scatter")

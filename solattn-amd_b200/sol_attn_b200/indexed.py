@@ -1,8 +1,10 @@
-"""Explicit equal-length indexed windows (mirrors ``src/sol_attn_amd/indexed.py``).
+"""Explicit indexed windows (mirrors ``src/sol_attn_amd/indexed.py``).
 
 ``IndexedPlan`` keeps the reference's fields, validation and messages; its protection matrix
 is built with sorted-index searches instead of the reference's Python double loop over
-(key block, query block) (``indexed.py:52-61``), with identical results.
+(key block, query block) (``indexed.py:52-61``), with identical results.  As an extension the
+windows may have different key counts (``keys`` given as one 1-D tensor per window): one plan
+and one launch then cover windows that the reference needs a separate plan each for.
 ``sol_attention_indexed`` does not materialise gathered Q/K/V copies: the plan's row and key
 indices are handed to the kernels, which gather rows while pooling and while loading tiles.
 """
@@ -11,6 +13,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
+from typing import Optional
 
 import torch
 
@@ -63,14 +66,29 @@ class IndexedPlan:
     keys: torch.Tensor
     protected_blocks: torch.Tensor
     sequence_length: int
+    # Ragged plans only: int32 [W] key count of each window; ``keys`` is then padded to the
+    # longest window (with the window's last key, never read) and ``protected_blocks`` to its
+    # block count (False).  None for the reference's rectangular plans.
+    key_counts: Optional[torch.Tensor] = None
 
     @classmethod
     def create(cls, rows, keys, sequence_length, *, protected_ranges=(), local_tokens=64):
+        """``keys`` is a [W, nk] matrix (the reference's form) or, as an extension, a list of
+        W 1-D tensors with per-window lengths (a ragged plan)."""
         _nonnegative_integer("local_tokens", local_tokens)
         _nonnegative_integer("sequence_length", sequence_length)
         if sequence_length == 0:
             raise ValueError("sequence_length must be positive")
-        for name, x in (("rows", rows), ("keys", keys)):
+        ragged = isinstance(keys, (list, tuple))
+        key_rows = list(keys) if ragged else None
+        if ragged:
+            if not key_rows or any(not isinstance(x, torch.Tensor) or x.ndim != 1
+                                   for x in key_rows):
+                raise ValueError("keys must be a nonempty CPU int64 matrix")
+            checks = [("rows", rows)] + [("keys", x[None]) for x in key_rows]
+        else:
+            checks = [("rows", rows), ("keys", keys)]
+        for name, x in checks:
             if (x.device.type != "cpu" or x.dtype != torch.int64 or x.ndim != 2
                     or any(n == 0 for n in x.shape)):
                 raise ValueError(f"{name} must be a nonempty CPU int64 matrix")
@@ -78,19 +96,34 @@ class IndexedPlan:
                 raise ValueError(f"{name} index outside sequence")
             if bool((x[:, 1:] <= x[:, :-1]).any()):
                 raise ValueError(f"{name} must be strictly increasing within each batch")
-        if rows.shape[0] != keys.shape[0]:
+        if rows.shape[0] != (len(key_rows) if ragged else keys.shape[0]):
             raise ValueError("rows and keys must have the same batch size")
         ranges = tuple(protected_ranges)
         for a, b in ranges:
             if not (isinstance(a, int) and isinstance(b, int)
                     and 0 <= a < b <= sequence_length):
                 raise ValueError("Invalid protected key range")
-        protection = build_protection(rows, keys, sequence_length, ranges, local_tokens)
-        return cls(rows.clone().contiguous(), keys.clone().contiguous(), protection, sequence_length)
+        if not ragged:
+            protection = build_protection(rows, keys, sequence_length, ranges, local_tokens)
+            return cls(rows.clone().contiguous(), keys.clone().contiguous(), protection,
+                       sequence_length)
+        # Ragged: each window's protection exactly as its own rectangular plan, padded.
+        counts = torch.tensor([x.numel() for x in key_rows], dtype=torch.int32)
+        nk = int(counts.max())
+        nqb, nkb = (rows.shape[1] + BLOCK - 1) // BLOCK, (nk + BLOCK - 1) // BLOCK
+        padded = torch.empty((len(key_rows), nk), dtype=torch.int64)
+        protection = torch.zeros((len(key_rows), nqb, nkb), dtype=torch.bool)
+        for w, x in enumerate(key_rows):
+            padded[w, :x.numel()] = x
+            padded[w, x.numel():] = x[-1]
+            own = build_protection(rows[w:w + 1], x[None], sequence_length, ranges, local_tokens)
+            protection[w, :, :own.shape[2]] = own[0]
+        return cls(rows.clone().contiguous(), padded, protection, sequence_length, counts)
 
     def to(self, device):
         return IndexedPlan(self.rows.to(device), self.keys.to(device),
-                           self.protected_blocks.to(device), self.sequence_length)
+                           self.protected_blocks.to(device), self.sequence_length,
+                           None if self.key_counts is None else self.key_counts.to(device))
 
 
 def sol_attention_indexed(q, k, v, plan, *, beta=1.0, scale=None, return_stats=False,
@@ -121,13 +154,20 @@ def sol_attention_indexed(q, k, v, plan, *, beta=1.0, scale=None, return_stats=F
             or plan.protected_blocks.shape != (b, (nq + 63) // 64, (plan.keys.shape[1] + 63) // 64)
             or any(not x.is_contiguous() for x in (plan.rows, plan.keys, plan.protected_blocks))):
         raise ValueError("Invalid indexed descriptor; use IndexedPlan.create")
+    kc = plan.key_counts
+    if kc is not None and (kc.dtype != torch.int32 or tuple(kc.shape) != (b,)
+                           or kc.device != q.device or not kc.is_contiguous()):
+        raise ValueError("Invalid indexed descriptor; use IndexedPlan.create")
     beta = float(beta)
     if math.isnan(beta):
         raise ValueError("beta must not be NaN")
     out = _check_out(out, q)
     with torch.no_grad(), torch.cuda.device(q.device):
         out, counts = launch_sol(q, k, v, scale, beta, -1, 0, 0, return_stats,
-                                 plan.protected_blocks, rows=plan.rows, keys=plan.keys, out=out)
+                                 plan.protected_blocks, rows=plan.rows, keys=plan.keys, out=out,
+                                 key_counts=kc)
     if return_stats:
-        return out, SolStats(counts, (plan.keys.shape[1] + 63) // 64)
+        key_blocks = ((plan.keys.shape[1] + 63) // 64 if kc is None
+                      else ((kc + 63) // 64).view(b, 1, 1))
+        return out, SolStats(counts, key_blocks)
     return out

@@ -106,3 +106,28 @@ def test_dense_attention_rows_matches_sdpa_and_gathered_dense():
     assert bool((out[untouched] == -5.0).all())
     fresh = dense_attention_rows(q, k, v, rows)
     assert torch.equal(fresh[rows], out[rows])
+
+
+def test_ragged_plan_equals_separate_window_plans():
+    """One launch over windows with different key counts gives, bit for bit, what one
+    rectangular plan per window gives (outputs, exact-block counts), also with scatter."""
+    from test_plan import ragged_fixture
+    rows, keys = ragged_fixture()
+    ranges = ((0, 7), (1180, 1193))
+    g = torch.Generator().manual_seed(11)
+    q, k, v = (torch.randn((1200, 2, 128), generator=g, dtype=torch.bfloat16).cuda()
+               for _ in range(3))
+    p = IndexedPlan.create(rows, keys, 1200, protected_ranges=ranges, local_tokens=64).to("cuda")
+    for beta in (1.0, 0.0, -math.inf, math.inf):
+        out, stats = sol_attention_indexed(q, k, v, p, beta=beta, return_stats=True)
+        scat = torch.zeros_like(q)
+        sol_attention_indexed(q, k, v, p, beta=beta, out=scat)
+        for w, x in enumerate(keys):
+            own = IndexedPlan.create(rows[w:w + 1], x[None], 1200, protected_ranges=ranges,
+                                     local_tokens=64).to("cuda")
+            o1, s1 = sol_attention_indexed(q, k, v, own, beta=beta, return_stats=True)
+            assert torch.equal(out[w], o1[0]), (beta, w)
+            assert torch.equal(stats.exact_blocks[w], s1.exact_blocks[0]), (beta, w)
+            assert torch.equal(scat[rows[w].cuda()], o1[0]), (beta, w)
+    d = stats.density()
+    assert 0.0 < d <= 1.0

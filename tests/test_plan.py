@@ -89,3 +89,43 @@ def test_protection_fuzz_against_loop_restatement():
 def test_plan_to_keeps_fields():
     p = fixture().to("cpu")
     assert p.sequence_length == 509 and p.rows.is_contiguous() and p.keys.dtype == torch.int64
+
+
+def ragged_fixture():
+    """Three windows of 96 queries whose key sets have 200, 70 and 131 keys."""
+    g = torch.Generator().manual_seed(3)
+    rows = torch.stack([torch.arange(s, s + 96) for s in (10, 400, 900)])
+    keys = [torch.sort(torch.randperm(1200, generator=g)[:n]).values for n in (200, 70, 131)]
+    return rows, keys
+
+
+def test_ragged_plan_matches_per_window_plans():
+    """A ragged plan (per-window key counts, an extension) pads keys with each window's last
+    key and protection with False, and each window's protection equals its own plan's."""
+    rows, keys = ragged_fixture()
+    ranges = ((0, 7), (1180, 1193))
+    p = IndexedPlan.create(rows, keys, 1200, protected_ranges=ranges, local_tokens=64)
+    assert p.key_counts.tolist() == [200, 70, 131]
+    assert p.key_counts.dtype == torch.int32
+    assert p.keys.shape == (3, 200) and p.protected_blocks.shape == (3, 2, 4)
+    for w, x in enumerate(keys):
+        own = IndexedPlan.create(rows[w:w + 1], x[None], 1200, protected_ranges=ranges,
+                                 local_tokens=64)
+        n, nb = x.numel(), (x.numel() + 63) // 64
+        assert torch.equal(p.keys[w, :n], x) and bool((p.keys[w, n:] == x[-1]).all())
+        assert torch.equal(p.protected_blocks[w, :, :nb], own.protected_blocks[0])
+        assert not p.protected_blocks[w, :, nb:].any()
+    rect = IndexedPlan.create(rows, torch.stack([k[:70] for k in keys]), 1200)
+    assert rect.key_counts is None
+
+
+def test_ragged_plan_rejects_invalid_windows():
+    rows, keys = ragged_fixture()
+    with pytest.raises(ValueError, match="strictly increasing"):
+        IndexedPlan.create(rows, [keys[0], keys[1].flip(0), keys[2]], 1200)
+    with pytest.raises(ValueError, match="same batch size"):
+        IndexedPlan.create(rows, keys[:2], 1200)
+    with pytest.raises(ValueError, match="nonempty"):
+        IndexedPlan.create(rows, [keys[0], keys[1][:0], keys[2]], 1200)
+    with pytest.raises(ValueError, match="nonempty"):
+        IndexedPlan.create(rows, [], 1200)
