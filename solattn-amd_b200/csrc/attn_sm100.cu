@@ -95,9 +95,9 @@ struct Layout {
   static constexpr int kV = kK + kStages * kKVTile;
   static constexpr int kBars = kV + kStages * kKVTile;
   // uint32 [0] TMEM address [1] abort flag; of list buffer j: [2 + j] tiles (even), [4 + j]
-  // item, [6 + j] tiles with keys (the rest is one padding tile)
+  // item, [6 + j] tiles with keys (the rest is one padding tile), [8 + j] the item's key count
   static constexpr int kMisc = kBars + NBARS * 8;
-  static constexpr int kMerge = kMisc + 32;  // float [2 items][8 warps][2][32 lanes]: m, l
+  static constexpr int kMerge = kMisc + 48;  // float [2 items][8 warps][2][32 lanes]: m, l
   static constexpr int kMask = kMerge + 2 * 8 * 2 * 32 * 4;  // uint32 [2 items][2 q-blocks][nwords]
   __host__ __device__ static int tiles_offset(int nwords) { return kMask + 4 * nwords * 4; }
   __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + nkb + 1; }
@@ -277,9 +277,9 @@ __device__ __forceinline__ MaskWords load_mask_words(const AttnParams& p, int it
 // per-q-block exact counts when requested and returns the number of tiles (warp-uniform).
 __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPos& ip,
                                                const MaskWords& mw, uint32_t* m, int16_t* tiles,
-                                               int nwords, int lane) {
+                                               int nwords, int tk, int lane) {
   const bool has1 = ip.qb0 + 1 < p.nqb;
-  const int nkb_b = (key_count(p, ip.b) + kBlock - 1) / kBlock;  // this batch's key blocks
+  const int nkb_b = (tk + kBlock - 1) / kBlock;  // this batch's key blocks
   if (p.masks) {
 #pragma unroll
     for (int j = 0; j < kMaskRegs; ++j)
@@ -561,11 +561,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       int16_t* tl = sTiles + lb * max_tiles;
-      const int ntiles = build_tile_list(p, ip, mw, sMask + lb * 2 * nwords, tl, nwords, lane);
+      const int tk = key_count(p, ip.b);  // the item's keys (its window's count if ragged)
+      const int ntiles = build_tile_list(p, ip, mw, sMask + lb * 2 * nwords, tl, nwords, tk, lane);
       if (lane == 0) {
         misc[2 + lb] = (uint32_t)ntiles;
         misc[4 + lb] = (uint32_t)item;
         misc[6 + lb] = (uint32_t)(ntiles - (tl[ntiles - 1] == kDummyTile ? 1 : 0));
+        misc[8 + lb] = (uint32_t)tk;
         mbar_arrive(bar(LIST_FULL + lb));
       }
       mw = load_mask_words(p, next, total, nwords, lane);
@@ -598,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto row_idx = [&](int e) {
           RowIdx<kKeys> ri;
           if (e >= 0) {
-            ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, key_count(p, ip.b) - e * kBlock, lane,
+            ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, tk - e * kBlock, lane,
                                      p.status);
           } else {
             ri.t[0] = ri.t[1] = 0;
@@ -784,7 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The warp's q-block exists (only the last pair of a head can lack its second q-block).
       const bool warp_rows = qsel == 0 || ip.qb0 + 1 < p.nqb;
       // The batch's keys (its own count in a ragged launch) and its last, maybe partial, block.
-      const int tk = key_count(p, ip.b), nkb_b = (tk + kBlock - 1) / kBlock;
+      const int tk = (int)vmisc[8 + lb], nkb_b = (tk + kBlock - 1) / kBlock;
       const int last_len = tk - (nkb_b - 1) * kBlock;
       const float last_bias = log2f((float)last_len);
       const int last_col = (nkb_b - 1) & 63;  // column of the last centroid in its group
