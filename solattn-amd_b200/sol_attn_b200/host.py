@@ -66,8 +66,9 @@ def sol_attention_host(q, k, v, *, beta=1.0, scale=None, local_blocks=1, kv_sink
     [sB, sT, D, 1]; rows may be spaced, as in a packed QKV buffer).  ``out``: an optional
     preallocated CPU BF16 tensor of q's shape with the same rule (pinned for overlap).  ``device``: the
     B200 to use (default: the current CUDA device).  ``heads_per_group``: heads per pipeline
-    stage (default H // 8, at least 1: eight stages keep the first copy-in and the last
-    copy-out, which nothing overlaps, short).  Blocks until the output is in host memory.
+    stage (default: one head in the first and the last stage, whose copy-in and copy-out
+    nothing overlaps, and about eleven equal stages in between).  Blocks until the output is
+    in host memory.
     """
     for name, x in (("q", q), ("k", k), ("v", v)):
         if x.device.type != "cpu":
@@ -98,10 +99,23 @@ def sol_attention_host(q, k, v, *, beta=1.0, scale=None, local_blocks=1, kv_sink
           or out.stride(-1) != 1 or out.stride(2) != D):
         raise ValueError("out must be a CPU BF16 tensor of q's shape with contiguous heads "
                          "within each row")
-    hg = max(1, H // 8) if heads_per_group is None else int(heads_per_group)
-    if hg <= 0:
-        raise ValueError("heads_per_group must be positive")
-    groups = [(h0, min(H, h0 + hg)) for h0 in range(0, H, hg)]
+    if heads_per_group is None:
+        # Tapered: the first copy-in and the last copy-out overlap nothing, so the first and
+        # last groups hold one head; about eleven groups in between keep the per-group launch
+        # costs small against the copies.
+        mid = max(1, -(-(H - 2) // 11)) if H >= 4 else 1
+        sizes = [1] + [mid] * ((H - 2) // mid) + ([(H - 2) % mid] if (H - 2) % mid else []) + [1] \
+            if H >= 4 else [1] * H
+    else:
+        hgi = int(heads_per_group)
+        if hgi <= 0:
+            raise ValueError("heads_per_group must be positive")
+        sizes = [min(hgi, H - h0) for h0 in range(0, H, hgi)]
+    groups, h0 = [], 0
+    for n in sizes:
+        groups.append((h0, h0 + n))
+        h0 += n
+    hg = max(sizes)
     nqb = (Tq + BLOCK - 1) // BLOCK
     from .attention import _validate, launch_sol  # noqa: PLC0415 (device-side checks)
 
