@@ -62,8 +62,8 @@ SOLATTN_API const char* solattn_strerror(int code);
  * Scratch layout of one forward call.  Replaces the torch.empty allocations of the
  * reference launcher (kernels.py:185-190, 203-217): kc/vc (BF16 K/V block means), qc (FP32
  * Q block means), mean/var (FP32 key moments), cutoff (FP32 Eq. 15 thresholds), one device
- * status word, and masks (the routing decisions, uint32 bitmask [B, H, nqb, ceil(nkb/32)],
- * followed by one uint32 work counter).
+ * status word, and masks (solattn_masks_bytes(): the routing decisions, uint32 bitmask
+ * [B, H, nqb, ceil(nkb/32)], then the fused kernel's work counter and per-item tile lists).
  * Offsets are in bytes from the workspace base, each 256-byte aligned.  The pooled tensors
  * use the layout [B, H, blocks, D]; cutoff is [B, H, nqb].
  * Returns the total size in bytes, or 0 on an invalid shape.
@@ -106,6 +106,9 @@ SOLATTN_API int solattn_threshold(const void* kc, const float* qc, int64_t B, in
                       int64_t nkb, int64_t D, float scale, float beta, float* mean, float* var,
                       float* cutoff, void* stream);
 
+/* Bytes of the `masks` buffer of solattn_attention (0 on an invalid shape). */
+SOLATTN_API int64_t solattn_masks_bytes(int64_t B, int64_t Tq, int64_t Tk, int64_t H);
+
 /*
  * Fused routed attention.  Replaces `_sol` (kernels.py:101-182, launch 216-224): per
  * (b, h, 64-row q-block) it routes every key block (threshold / force mode, OR the local
@@ -116,9 +119,10 @@ SOLATTN_API int solattn_threshold(const void* kc, const float* qc, int64_t B, in
  * force != 0.  counts may be NULL.  status may be NULL.
  * masks receives the routing decisions as a bitmask [B, H, nqb, ceil(nkb/32)] of uint32
  * words (bit kb%32 of word kb/32 set = block kb exact); the call writes it in a routing pass
- * and the attention kernel reads it back.  The buffer holds B*H*nqb*ceil(nkb/32) + 1 words:
- * the last one is the attention kernel's work counter (zeroed by the routing pass, then
- * incremented as the persistent CTAs take work items).  It is required when
+ * and the attention kernel reads it back.  The buffer (16-byte aligned) holds
+ * solattn_masks_bytes(B, Tq, Tk, H) bytes: the bitmask, then the attention kernel's work
+ * counter (zeroed by the routing pass, then incremented as the persistent CTAs take work
+ * items) and one tile list per q-block pair (built by the routing pass).  It is required when
  * force == SOLATTN_FORCE_THRESHOLD and may be NULL in the force modes (the rules are then
  * evaluated inside the kernel and the work is split round robin).
  */
@@ -220,7 +224,7 @@ SOLATTN_API int solattn_dense(const void* q, const void* k, const void* v,
  * program that owns all device memory through its own pool and forbids direct cudaMalloc, or a
  * latency-critical loop that cannot afford cudaMalloc's implicit synchronisation.  Same
  * arguments and results as solattn_sol_forward minus the workspace: the scratch is a fixed
- * file-scope device array of solattn_noalloc_scratch_bytes() bytes (16 MiB) that every GPU
+ * file-scope device array of solattn_noalloc_scratch_bytes() bytes (32 MiB) that every GPU
  * loading this library holds until the process exits.  Problems whose
  * solattn_workspace_layout() size exceeds it return SOLATTN_ERR_TOO_LARGE before any GPU work.
  * All calls on a device share that array and it keeps the last call's contents (the status

@@ -71,7 +71,7 @@ constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
 // their item-local parity: the result of an item then does not depend on which CTA ran it
 // after which other items (bitwise repeatable under the dynamic schedule).  No keys, no loads,
 // no MMAs, P = 0.  Centroid entries are -(t + 1) >= -64.
-constexpr int kDummyTile = -32768;
+constexpr int kDummyTile = kPadTile;
 // Readers of an item's tile list that must be done before the producer overwrites it two items
 // later: the softmax warps, the two S issuers and the P V issuer.
 constexpr int kListReaders = kSoftmaxWarps + 3;
@@ -100,7 +100,7 @@ struct Layout {
   static constexpr int kMerge = kMisc + 48;  // float [2 items][8 warps][2][32 lanes]: m, l
   static constexpr int kMask = kMerge + 2 * 8 * 2 * 32 * 4;  // uint32 [2 items][2 q-blocks][nwords]
   __host__ __device__ static int tiles_offset(int nwords) { return kMask + 4 * nwords * 4; }
-  __host__ __device__ static int max_tiles(int nkb) { return (nkb + kKeys - 1) / kKeys + nkb + 1; }
+  __host__ __device__ static int max_tiles(int nkb) { return item_list_capacity(nkb); }
   static size_t bytes(int nkb) {  // int16 tile lists [2 items][max_tiles]
     const int nwords = (nkb + 31) / 32;
     return 1024 + (size_t)tiles_offset(nwords) + 2 * (size_t)max_tiles(nkb) * 2;
@@ -251,14 +251,22 @@ __device__ __forceinline__ ItemPos item_pos(const AttnParams& p, int item) {
 constexpr int kMaskRegs = 2 * (kMaxKeyBlocks / 32) / 32;
 struct MaskWords {
   uint32_t w[kMaskRegs];
+  int ntiles, real;  // from the item's precomputed list header (when the routing pass built it)
 };
 __device__ __forceinline__ MaskWords load_mask_words(const AttnParams& p, int item, int total,
                                                      int nwords, int lane) {
   MaskWords mw;
 #pragma unroll
   for (int j = 0; j < kMaskRegs; ++j) mw.w[j] = 0u;
+  mw.ntiles = mw.real = 0;
   if (!p.masks || item >= total) return mw;
   const ItemPos ip = item_pos(p, item);
+  if (p.lists) {
+    const int2 hdr = __ldg(reinterpret_cast<const int2*>(
+        p.lists + ((int64_t)ip.bh * ((p.nqb + 1) / 2) + (ip.qb0 >> 1)) * item_list_stride(p.nkb)));
+    mw.ntiles = hdr.x;
+    mw.real = hdr.y;
+  }
 #pragma unroll
   for (int j = 0; j < kMaskRegs; ++j) {
     const int i = 32 * j + lane;
@@ -272,12 +280,12 @@ __device__ __forceinline__ MaskWords load_mask_words(const AttnParams& p, int it
 
 // One warp: both q-blocks' exact-block bitmasks of an item into m[0, 2 nwords) -- the routing
 // pass's words (loaded ahead into `mw`), or (force modes without a mask buffer) the force /
-// local / sink / protected rules alone -- then the item's tile list into `tiles`: the useful
-// 64-centroid groups, then the union of both exact sets in increasing order.  Writes the
-// per-q-block exact counts when requested and returns the number of tiles (warp-uniform).
+// local / sink / protected rules alone.  Then, without a precomputed list, the item's tile list
+// into `tiles` (build_item_list) and the per-q-block exact counts when requested; returns the
+// number of tiles (warp-uniform) and the count without the padding entry in `real`.
 __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPos& ip,
                                                const MaskWords& mw, uint32_t* m, int16_t* tiles,
-                                               int nwords, int tk, int lane) {
+                                               int nwords, int tk, int lane, int& real) {
   const bool has1 = ip.qb0 + 1 < p.nqb;
   const int nkb_b = (tk + kBlock - 1) / kBlock;  // this batch's key blocks
   if (p.masks) {
@@ -293,54 +301,16 @@ __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPo
     }
   }
   __syncwarp();
-  const uint32_t* m0 = m;
-  const uint32_t* m1 = m + nwords;
-  int n = 0;
-  const int nct = p.force == 1 ? 0 : (nkb_b + kKeys - 1) / kKeys;
-  for (int t0 = 0; t0 < nct; t0 += 32) {
-    const int t = t0 + lane;
-    bool useful = false;
-    if (t < nct) {
-      for (int wi = 2 * t; wi < 2 * t + 2 && wi < nwords; ++wi) {
-        const uint32_t v = valid_word(wi, nkb_b);
-        if ((~m0[wi] & v) || (has1 && (~m1[wi] & v))) useful = true;
-      }
-    }
-    const uint32_t bal = __ballot_sync(0xffffffffu, useful);
-    if (useful) tiles[n + __popc(bal & ((1u << lane) - 1u))] = (int16_t)(-(t + 1));
-    n += __popc(bal);
+  if (p.lists) {  // the routing pass built the list (and wrote the counts)
+    real = mw.real;
+    return mw.ntiles;
   }
-  int r = 0;
-  for (int w0 = 0; w0 < nwords; w0 += 32) {
-    const int wi = w0 + lane;
-    uint32_t bits = 0u;
-    if (wi < nwords) bits = m0[wi] | (has1 ? m1[wi] : 0u);
-    const int cnt = __popc(bits);
-    int incl = cnt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    int rank = n + r + incl - cnt;
-    while (bits) {
-      const int bit = __ffs(bits) - 1;
-      bits &= bits - 1u;
-      tiles[rank++] = (int16_t)(32 * wi + bit);
-    }
-    r += __shfl_sync(0xffffffffu, incl, 31);
-  }
+  const int n = build_item_list(m, m + nwords, has1, nwords, nkb_b, p.force, tiles, lane, real);
   if (lane < 2 && p.counts && ip.qb0 + lane < p.nqb) {
     int c = 0;
     for (int i = 0; i < nwords; ++i) c += __popc(m[lane * nwords + i]);
     p.counts[((int64_t)ip.b * p.nqb + ip.qb0 + lane) * p.H + ip.h] = c;
   }
-  n += r;
-  if (n & 1) {  // even tile counts: every item starts at an even tile position
-    if (lane == 0) tiles[n] = (int16_t)kDummyTile;
-    ++n;
-  }
-  __syncwarp();
   return n;
 }
 
@@ -562,15 +532,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int16_t* tl = sTiles + lb * max_tiles;
       const int tk = key_count(p, ip.b);  // the item's keys (its window's count if ragged)
-      const int ntiles = build_tile_list(p, ip, mw, sMask + lb * 2 * nwords, tl, nwords, tk, lane);
+      int real;
+      const int ntiles =
+          build_tile_list(p, ip, mw, sMask + lb * 2 * nwords, tl, nwords, tk, lane, real);
       if (lane == 0) {
         misc[2 + lb] = (uint32_t)ntiles;
         misc[4 + lb] = (uint32_t)item;
-        misc[6 + lb] = (uint32_t)(ntiles - (tl[ntiles - 1] == kDummyTile ? 1 : 0));
+        misc[6 + lb] = (uint32_t)real;
         misc[8 + lb] = (uint32_t)tk;
-        mbar_arrive(bar(LIST_FULL + lb));
+        if (p.lists) {
+          // The routing pass's list for this item: one bulk copy, which completes the barrier.
+          const uint32_t bytes = (uint32_t)((2 * ntiles + 15) & ~15);
+          const uint8_t* src = p.lists + 16 +
+              ((int64_t)ip.bh * ((p.nqb + 1) / 2) + (ip.qb0 >> 1)) * item_list_stride(p.nkb);
+          mbar_expect_tx(bar(LIST_FULL + lb), bytes);
+          bulk_copy_g2s(smem_u32(tl), src, bytes, bar(LIST_FULL + lb));
+        } else {
+          mbar_arrive(bar(LIST_FULL + lb));
+        }
       }
       mw = load_mask_words(p, next, total, nwords, lane);
+      // The producer reads the list too (its K/V loads follow the entries).
+      if (p.lists && !warp_wait(bar(LIST_FULL + lb), (uint32_t)(k >> 1) & 1u, abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
       // K and V tiles of the item
       if (!p.k.idx) {
         if (lane == 0) {

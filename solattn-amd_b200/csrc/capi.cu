@@ -59,6 +59,22 @@ struct Layout {
   int64_t kc, vc, qc, mean, var, cutoff, masks, status, total;
 };
 
+// Bytes of the routing-mask buffer: the bitmask words, the work counter (padded to 16 bytes),
+// then one tile list per q-block pair (common.cuh: item_list_stride).
+int64_t masks_bytes(int64_t B, int64_t Tq, int64_t Tk, int64_t H) {
+  const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
+  const int64_t words = (B * H * nqb * cdiv(nkb, 32) + 1 + 3) & ~int64_t(3);
+  return 4 * words + B * H * cdiv(nqb, 2) * item_list_stride((int)nkb);
+}
+
+// The tile lists inside a mask buffer.
+uint8_t* lists_of(uint32_t* masks, int64_t B, int64_t Tq, int64_t Tk, int64_t H) {
+  if (!masks) return nullptr;
+  const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
+  const int64_t words = (B * H * nqb * cdiv(nkb, 32) + 1 + 3) & ~int64_t(3);
+  return reinterpret_cast<uint8_t*>(masks) + 4 * words;
+}
+
 Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   Layout L;
   const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
@@ -78,7 +94,7 @@ Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   L.cutoff = off;
   off = align256(off + B * H * nqb * 4);
   L.masks = off;
-  off = align256(off + B * H * nqb * cdiv(nkb, 32) * 4 + 4);  // + the work counter
+  off = align256(off + masks_bytes(B, Tq, Tk, H));  // + the work counter and tile lists
   L.total = off;
   return L;
 }
@@ -126,6 +142,11 @@ int64_t solattn_workspace_layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, i
   if (off_status) *off_status = L.status;
   if (off_masks) *off_masks = L.masks;
   return L.total;
+}
+
+int64_t solattn_masks_bytes(int64_t B, int64_t Tq, int64_t Tk, int64_t H) {
+  if (B <= 0 || Tq <= 0 || Tk <= 0 || H <= 0) return 0;
+  return masks_bytes(B, Tq, Tk, H);
 }
 
 int solattn_pool_qkv(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
@@ -201,6 +222,7 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
   if (rc) return rc;
   if (!q || !k || !v || !kc || !vc || !out) return SOLATTN_ERR_ARG;
   if (force == SOLATTN_FORCE_THRESHOLD && !masks) return SOLATTN_ERR_ARG;
+  if (masks && !aligned16(masks)) return SOLATTN_ERR_ARG;
   if (out_idx && out_rows <= 0) return SOLATTN_ERR_ARG;
   if (key_counts && !kv_idx) return SOLATTN_ERR_ARG;  // ragged key counts: indexed inputs only
   if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
@@ -228,6 +250,7 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
   p.counts = counts;
   p.status = status;
   p.masks = masks;
+  p.lists = lists_of(masks, B, Tq, Tk, H);
   p.B = (int)B;
   p.Tq = (int)Tq;
   p.Tk = (int)Tk;

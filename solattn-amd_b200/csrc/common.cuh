@@ -39,6 +39,8 @@ struct AttnParams {
   int32_t* status;          // device status word or nullptr
   uint32_t* masks;          // [B, H, nqb, ceil(nkb/32)] routing bitmask: written by route.cu
                             // (read by attn_sm100_kernel) or by attn_mma_kernel
+  uint8_t* lists;           // per-item tile lists (see item_list_stride) written by route.cu, or
+                            // nullptr (the fused kernel then builds them itself)
   int B, Tq, Tk, H, nqb, nkb;
   const int32_t* tk_b;  // optional per-batch key counts [B] (ragged indexed plans: batch b has
                         // tk_b[b] <= Tk keys, ceil(tk_b[b] / 64) key blocks), else nullptr
@@ -184,6 +186,80 @@ __device__ __forceinline__ void routing_dot2(const float* qa, const float* qb,
                  __fadd_rn(__fadd_rn(pa[4], pa[5]), __fadd_rn(pa[6], pa[7])));
   db = __fadd_rn(__fadd_rn(__fadd_rn(pb[0], pb[1]), __fadd_rn(pb[2], pb[3])),
                  __fadd_rn(__fadd_rn(pb[4], pb[5]), __fadd_rn(pb[6], pb[7])));
+}
+
+// Tile lists of the fused sm_100 kernel, one per item = q-block pair (b, h, pair): a 16-byte
+// header {tiles (even), tiles with keys, 0, 0} and item_list_capacity(nkb) int16 entries:
+// first every 64-centroid group that still has a block unselected by either q-block (entry
+// -(t + 1)), then every block of the union of both q-blocks' exact sets in increasing order
+// (entry kb >= 0), then, for an odd count, one padding entry.  Capacities are multiples of 8
+// entries so that every list starts on a 16-byte boundary.
+constexpr int kPadTile = -32768;  // the padding entry (centroid entries are -(t + 1) >= -64)
+__host__ __device__ inline int item_list_capacity(int nkb) {
+  return ((nkb + 63) / 64 + nkb + 1 + 7) & ~7;
+}
+__host__ __device__ inline int64_t item_list_stride(int nkb) {
+  return 16 + 2 * (int64_t)item_list_capacity(nkb);
+}
+
+__device__ __forceinline__ uint32_t valid_bits32(int w, int nkb) {
+  const int lo = 32 * w;
+  if (lo + 32 <= nkb) return 0xffffffffu;
+  if (lo >= nkb) return 0u;
+  return (1u << (nkb - lo)) - 1u;
+}
+
+// One warp: the tile list of a q-block pair from the two q-blocks' exact-block bitmasks m0 and
+// m1 (nwords words each; m1 is ignored when has1 is false) into `tiles` (shared or global
+// memory), padded to an even count.  Returns the count (warp-uniform); `real` receives the
+// count without the padding entry.  nkb_b: key blocks of the batch; force == 1 (every block
+// exact) lists no centroid group.
+__device__ __forceinline__ int build_item_list(const uint32_t* m0, const uint32_t* m1, bool has1,
+                                               int nwords, int nkb_b, int force, int16_t* tiles,
+                                               int lane, int& real) {
+  int n = 0;
+  const int nct = force == 1 ? 0 : (nkb_b + 63) / 64;
+  for (int t0 = 0; t0 < nct; t0 += 32) {
+    const int t = t0 + lane;
+    bool useful = false;
+    if (t < nct) {
+      for (int wi = 2 * t; wi < 2 * t + 2 && wi < nwords; ++wi) {
+        const uint32_t v = valid_bits32(wi, nkb_b);
+        if ((~m0[wi] & v) || (has1 && (~m1[wi] & v))) useful = true;
+      }
+    }
+    const uint32_t bal = __ballot_sync(0xffffffffu, useful);
+    if (useful) tiles[n + __popc(bal & ((1u << lane) - 1u))] = (int16_t)(-(t + 1));
+    n += __popc(bal);
+  }
+  int r = 0;
+  for (int w0 = 0; w0 < nwords; w0 += 32) {
+    const int wi = w0 + lane;
+    uint32_t bits = 0u;
+    if (wi < nwords) bits = m0[wi] | (has1 ? m1[wi] : 0u);
+    const int cnt = __popc(bits);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int rank = n + r + incl - cnt;
+    while (bits) {
+      const int bit = __ffs(bits) - 1;
+      bits &= bits - 1u;
+      tiles[rank++] = (int16_t)(32 * wi + bit);
+    }
+    r += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  n += r;
+  real = n;
+  if (n & 1) {  // even tile counts: every item starts at an even tile position
+    if (lane == 0) tiles[n] = (int16_t)kPadTile;
+    ++n;
+  }
+  __syncwarp();
+  return n;
 }
 
 // Keys of batch b: its own count in a ragged launch (a count outside [1, Tk] is reported and

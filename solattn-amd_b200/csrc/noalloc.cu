@@ -9,7 +9,7 @@
 // and outputs, and this entry point needs nothing else.
 //
 // Cost and limits:
-//   - every GPU that loads libsolattn.so holds kNoAllocScratchBytes (16 MiB) of device memory
+//   - every GPU that loads libsolattn.so holds kNoAllocScratchBytes (32 MiB) of device memory
 //     for this array until the process exits;
 //   - problems whose workspace (solattn_workspace_layout) exceeds that size are rejected with
 //     SOLATTN_ERR_TOO_LARGE before any GPU work is enqueued;
@@ -27,7 +27,7 @@
 
 namespace {
 
-constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;
+constexpr int64_t kNoAllocScratchBytes = int64_t(32) << 20;
 constexpr int kMaxDevices = 128;
 
 }  // namespace

@@ -9,7 +9,10 @@
 // __fmul_rn / __fadd_rn, combined pairwise), so the decisions are bit-identical to the
 // per-CTA routing of the mma.sync kernel.  One ballot per q-block per 32 key blocks gives a
 // mask word: masks[((b * H + h) * nqb + qb) * nwords + kb / 32], bit kb % 32.  The word after
-// the last mask word is the fused attention kernel's work counter; the pass zeroes it.
+// the last mask word is the fused attention kernel's work counter; the pass zeroes it.  When a
+// list buffer is given the pass also builds every q-block pair's tile list for the fused kernel
+// (common.cuh: build_item_list) and writes the exact-block counts, so that no attention CTA
+// spends time on either between two items.
 #include "common.cuh"
 
 namespace solattn {
@@ -29,6 +32,8 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   const int nq = min(kRouteQB, p.nqb - qb_lo);
   const int nwords = (p.nkb + 31) / 32;
   const int nkb_b = (key_count(p, b) + kBlock - 1) / kBlock;  // this batch's key blocks
+  constexpr int kMaxWords = 4096 / 32;  // the fused kernel's limit of 4096 key blocks
+  __shared__ uint32_t smask[kRouteQB][kMaxWords];
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
     p.masks[(int64_t)p.B * p.H * p.nqb * nwords] = 0u;
   for (int i = threadIdx.x; i < kRouteQB * D; i += kRouteThreads) {
@@ -105,8 +110,29 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
       bool sel = false;
       if (kb < nkb_b) sel = route_rules(p, p.force == 0 && __fmul_rn(dot, p.scale) > scut[j], b, qb, kb);
       const uint32_t bal = __ballot_sync(0xffffffffu, sel);
-      if (lane == 0) p.masks[((int64_t)bh * p.nqb + qb) * nwords + w] = bal;
+      if (lane == 0) {
+        p.masks[((int64_t)bh * p.nqb + qb) * nwords + w] = bal;
+        if (nwords <= kMaxWords) smask[j][w] = bal;
+      }
     }
+  }
+  if (!p.lists || nwords > kMaxWords) return;
+  __syncthreads();
+  // Warp j: the tile list of the group's q-block pair j (q-blocks qb_lo + 2j, qb_lo + 2j + 1).
+  const int warp = threadIdx.x >> 5;
+  const int qb0 = qb_lo + 2 * warp;
+  if (warp >= kRouteQB / 2 || qb0 >= p.nqb) return;
+  const bool has1 = qb0 + 1 < p.nqb;
+  uint8_t* item =
+      p.lists + ((int64_t)bh * ((p.nqb + 1) / 2) + (qb0 >> 1)) * item_list_stride(p.nkb);
+  int real;
+  const int n = build_item_list(smask[2 * warp], smask[2 * warp + 1], has1, nwords, nkb_b,
+                                p.force, reinterpret_cast<int16_t*>(item + 16), lane, real);
+  if (lane == 0) *reinterpret_cast<int4*>(item) = make_int4(n, real, 0, 0);
+  if (lane < 2 && p.counts && qb0 + lane < p.nqb) {
+    int c = 0;
+    for (int i = 0; i < nwords; ++i) c += __popc(smask[2 * warp + lane][i]);
+    p.counts[((int64_t)b * p.nqb + qb0 + lane) * p.H + bh % p.H] = c;
   }
 }
 

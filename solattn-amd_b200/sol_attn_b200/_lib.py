@@ -44,6 +44,7 @@ SIGNATURES = {
                                     + [_P, _P, _I64, _P]
                                     + [c_float, c_float, c_int, c_int, c_int, _P, _P, _P]),
     "solattn_noalloc_scratch_bytes": (_I64, []),
+    "solattn_masks_bytes": (_I64, [_I64] * 4),
     "solattn_copy_2d": (c_int, [_P, _I64, _P, _I64, _I64, _I64, c_int, _P]),
 }
 

@@ -48,10 +48,12 @@ class Stages:
         self.out = torch.empty((B, Tq, H, D), dtype=bf16, device=dev)
         self.counts = torch.full((B, self.nqb, H), -1, dtype=torch.int32, device=dev) if counts else None
         # Routing decisions [B, H, nqb, ceil(nkb/32)] (bit kb % 32 of word kb / 32), written by
-        # the attention call's routing pass, followed by the attention kernel's work counter.
+        # the attention call's routing pass, followed by the attention kernel's work counter and
+        # the per-item tile lists (solattn_masks_bytes).
         nw = (self.nkb + 31) // 32
-        self._mask_words = torch.zeros(B * H * self.nqb * nw + 1, dtype=torch.int32, device=dev)
-        self.mask = self._mask_words[:-1].view(B, H, self.nqb, nw)
+        nbytes = int(self.L.solattn_masks_bytes(B, Tq, Tk, H))
+        self._mask_words = torch.zeros((nbytes + 3) // 4, dtype=torch.int32, device=dev)
+        self.mask = self._mask_words[:B * H * self.nqb * nw].view(B, H, self.nqb, nw)
 
     def _strides(self, x):
         return (0, x.stride(0), x.stride(1)) if self.indexed else (x.stride(0), x.stride(1), x.stride(2))

@@ -2,7 +2,7 @@
 
 It exists for callers that cannot obtain device memory when they call the operator (a plugin
 inside a host program that owns all device memory through its own pool, or a loop that cannot
-afford cudaMalloc's implicit synchronisation): its scratch is a fixed 16 MiB device array
+afford cudaMalloc's implicit synchronisation): its scratch is a fixed 32 MiB device array
 inside libsolattn.so rather than a caller-provided workspace.  These tests call it through the
 C ABI and check it against the workspace entry point ``solattn_sol_forward`` on the same
 inputs, on two calls in a row with different problems (the shared array keeps the previous
@@ -81,7 +81,7 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     """Rejected on the host, before any GPU work: no device is needed for this check."""
     L = _lib.load()
     limit = L.solattn_noalloc_scratch_bytes()
-    assert limit == 16 << 20
+    assert limit == 32 << 20
     B, T, H, D = 1, 65536, 64, 128
     assert _lib.workspace_layout(B, T, T, H, D)[0] > limit
     fake = 1 << 12  # never dereferenced: the size check fails first
