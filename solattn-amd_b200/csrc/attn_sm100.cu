@@ -96,9 +96,13 @@ struct Layout {
   static constexpr int kBars = kV + kStages * kKVTile;
   // uint32 [0] TMEM address [1] abort flag; of list buffer j: [2 + j] tiles (even), [4 + j]
   // item, [6 + j] tiles with keys (the rest is one padding tile), [8 + j] the item's key count
-  static constexpr int kMisc = kBars + NBARS * 8;
+  // Rounded up to 16 bytes: the tile lists behind it are filled by cp.async.bulk, whose shared
+  // destination must be 16-byte aligned whatever the number of barriers.
+  static constexpr int kMisc = (kBars + NBARS * 8 + 15) & ~15;
   static constexpr int kMerge = kMisc + 48;  // float [2 items][8 warps][2][32 lanes]: m, l
   static constexpr int kMask = kMerge + 2 * 8 * 2 * 32 * 4;  // uint32 [2 items][2 q-blocks][nwords]
+  static_assert(kMisc % 16 == 0 && kMerge % 16 == 0 && kMask % 16 == 0,
+                "tile lists must start on 16-byte boundaries (bulk-copy destination)");
   __host__ __device__ static int tiles_offset(int nwords) { return kMask + 4 * nwords * 4; }
   __host__ __device__ static int max_tiles(int nkb) { return item_list_capacity(nkb); }
   static size_t bytes(int nkb) {  // int16 tile lists [2 items][max_tiles]
