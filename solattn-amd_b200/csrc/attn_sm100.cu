@@ -1,7 +1,9 @@
 // Fused routed attention on the Blackwell data path (replaces `_sol`, kernels.py:101-182).
 //
 // Persistent kernel: one CTA per SM (it allocates all 512 TMEM columns) works through a list of
-// work items, item k of CTA c being item c + k * gridDim.x of the launch order.  An item is one
+// work items in launch order: CTA c starts with item c and takes each further item from the
+// launch's work counter while it issues the last tiles of the one before (round robin over the
+// grid when there is no counter).  An item is one
 // 128-row query tile = two 64-row q-blocks (qb0, qb0 + 1) of one (b, h).  Launch order: first
 // the q-block pairs holding query-sink blocks of all heads (every key block exact: the longest
 // items), then each head's remaining pairs head by head (the items in flight at one time share
@@ -66,6 +68,8 @@ constexpr uint32_t kTmemO = 0, kTmemS = 256;  // O_x at kTmemO + 128 x
 constexpr int kQBox = kRows * 128;   // one 128-row x 64-column BF16 box of Q (16 KB)
 constexpr int kKVBox = kKeys * 128;  // one 64-row x 64-column BF16 box of K or V (8 KB)
 constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
+constexpr int kClaimTiles = 8;       // late claim: the next item this many tiles before the end
+constexpr int kEarlyClaimItems = 16; // items per CTA from which the next items are claimed early
 // Tile-list entry that pads an item to an even tile count, so that every item starts at an even
 // position of the CTA's tile sequence and its tiles split between the two softmax groups by
 // their item-local parity: the result of an item then does not depend on which CTA ran it
@@ -484,11 +488,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // masks, zeroed by the routing pass) when there is one, else round robin over the grid.
     unsigned int* counter =
         p.masks ? p.masks + (int64_t)p.B * p.H * p.nqb * nwords : nullptr;
-    // The next item is claimed one item ahead and its mask words are loaded while the current
-    // item's tiles stream, so that neither latency falls between two items.
+    // When to claim the next item.  With many items per CTA (early): the item after next is
+    // claimed when an item starts, and the next item's mask words load while the current
+    // item's tiles stream, so that no latency falls between two items.  With few items per CTA
+    // (late): the next item is claimed while the producer issues the current item's last
+    // kClaimTiles tiles, about kClaimTiles + kStages tiles before the consumers can start it.
+    // A CTA then commits to an item only shortly before it is free for it, and the counter
+    // balances the CTAs' work up to the last items; claimed early, the last rounds of items
+    // are handed out by the state of the CTAs two items before, which leaves a tail of about
+    // one item (measured at 3 heads of the bench workload, 5 items per CTA: 7 % of the
+    // kernel's time; at 41 items per CTA the early claim is 0.7 % faster).
+    const bool early = total >= kEarlyClaimItems * (int)gridDim.x;
     int item = (int)blockIdx.x;
     int next = item + (int)gridDim.x;
-    if (counter && lane == 0) next = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+    if (early && counter && lane == 0) next = (int)gridDim.x + (int)atomicAdd(counter, 1u);
     next = __shfl_sync(0xffffffffu, next, 0);
     MaskWords mw = load_mask_words(p, item, total, nwords, lane);
     int g = 0;  // tiles of this CTA's earlier items
@@ -525,9 +538,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_4d(dq + j * kQBox, &tmQ, bar(Q_FULL + lb), 64 * j, ip.qb0 * kBlock, ip.h, ip.b);
       }
       ++q_issued;
-      // The item after next: claimed now, used two items on.
+      // Early claim: the item after next, used two items on.
       int next2 = next + (int)gridDim.x;
-      if (counter && lane == 0) next2 = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+      if (early && counter && lane == 0) next2 = (int)gridDim.x + (int)atomicAdd(counter, 1u);
       // The tile list, once the item two back has released the buffer.
       if (k >= 2 && !warp_wait(bar(LIST_EMPTY + lb), (uint32_t)((k >> 1) - 1) & 1u, abort_flag,
                                p.status)) {
@@ -555,33 +568,52 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(bar(LIST_FULL + lb));
         }
       }
-      mw = load_mask_words(p, next, total, nwords, lane);
+      if (early) mw = load_mask_words(p, next, total, nwords, lane);
       // The producer reads the list too (its K/V loads follow the entries).
       if (p.lists && !warp_wait(bar(LIST_FULL + lb), (uint32_t)(k >> 1) & 1u, abort_flag, p.status)) {
         ok = false;
         break;
       }
+      // Late claim of the next item: lane 0 issues the atomicAdd before tile claim_at and goes
+      // on issuing tiles; two tiles later, when the result has returned, the warp reads it and
+      // loads the item's mask words.
+      const int claim_at = max(0, ntiles - kClaimTiles);
+      const int read_at = min(ntiles, claim_at + 2);
+      int claimed = item + (int)gridDim.x;
+      auto claim_issue = [&]() {
+        if (!early && counter && lane == 0) claimed = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+      };
+      auto claim_read = [&]() {
+        if (early) return;
+        next = __shfl_sync(0xffffffffu, claimed, 0);
+        mw = load_mask_words(p, next, total, nwords, lane);
+      };
       // K and V tiles of the item
       if (!p.k.idx) {
-        if (lane == 0) {
-          for (int i = 0; i < ntiles; ++i) {
-            const int gi = g + i, s = gi % kStages;
-            const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;  // parity of the last use
-            if (gi >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
-              ok = false;
-              break;
+        const int bounds[4] = {0, claim_at, read_at, ntiles};
+        for (int phase = 0; phase < 3 && ok; ++phase) {
+          if (phase == 1) claim_issue();
+          if (phase == 2) claim_read();
+          if (lane == 0) {
+            for (int i = bounds[phase]; i < bounds[phase + 1]; ++i) {
+              const int gi = g + i, s = gi % kStages;
+              const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;  // parity of the last use
+              if (gi >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
+                ok = false;
+                break;
+              }
+              load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), tl[i], ip.h, ip.b);
+              ++k_issued;
+              if (gi >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
+                ok = false;
+                break;
+              }
+              load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), tl[i], ip.h, ip.b);
+              ++v_issued;
             }
-            load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), tl[i], ip.h, ip.b);
-            ++k_issued;
-            if (gi >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
-              ok = false;
-              break;
-            }
-            load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), tl[i], ip.h, ip.b);
-            ++v_issued;
           }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
       } else {
         // Gathered K/V rows: the whole warp copies; a tile's 64 row indices (shared by K and
         // V) are loaded one tile ahead.  Centroid tiles still come by TMA (lane 0), the other
@@ -599,6 +631,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         RowIdx<kKeys> ri = row_idx(ntiles > 0 ? tl[0] : -1);
         for (int i = 0; i < ntiles; ++i) {
+          if (i == claim_at) claim_issue();
+          if (i == read_at) claim_read();
           const int gi = g + i, s = gi % kStages;
           const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;
           const int e = tl[i];
@@ -620,10 +654,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++v_issued;
           if (i + 1 < ntiles) ri = row_idx(tl[i + 1]);
         }
+        if (ok && read_at == ntiles) {  // fewer than three tiles after claim_at
+          if (claim_at == ntiles) claim_issue();
+          claim_read();
+        }
       }
+      if (!ok) break;
       g += ntiles;
       item = next;
-      next = __shfl_sync(0xffffffffu, next2, 0);
+      if (early) next = __shfl_sync(0xffffffffu, next2, 0);
     }
     if (p.q.idx || p.k.idx) cp_async_wait_all();  // no copy may still write shared memory
     if (lane == 0 && *abort_flag) {

@@ -1,6 +1,8 @@
 // Key moments + Eq. 15 thresholds in one launch (replaces kernels.py:30-64, 211-215).
 //
-// One CTA per (b, h) and group of kThrQB q-blocks, D threads.  Thread d sums kc[b,h,:,d] and
+// One CTA per (b, h) and group of kThrQB q-blocks, D threads.  The head's centroid rows stream
+// through a ring of kRingStages shared-memory stages of kRingRows rows (16-byte cp.async, several
+// stages in flight, so the loads do not serialise with the sums).  Thread d sums kc[b,h,:,d] and
 // its squares over all key blocks in block order (FP32, no FMA), giving mean and population
 // variance var = max(E[x^2] - E[x]^2, 0) with every block weighted equally (kernels.py:40-47);
 // every CTA of a head computes the same moments (the first one writes them out).  The group's
@@ -15,7 +17,9 @@ namespace solattn {
 
 namespace {
 
-constexpr int kThrQB = 32;  // q-blocks per CTA
+constexpr int kThrQB = 32;      // q-blocks per CTA
+constexpr int kRingRows = 16;   // centroid rows per ring stage
+constexpr int kRingStages = 6;  // ring stages (kRingStages - 1 in flight)
 
 template <int D>
 __global__ void __launch_bounds__(D) threshold_kernel(const __nv_bfloat16* __restrict__ kc,
@@ -33,15 +37,39 @@ __global__ void __launch_bounds__(D) threshold_kernel(const __nv_bfloat16* __res
   const int d = threadIdx.x;
   for (int i = d; i < nq * D; i += D)
     s_q[i / D][i % D] = qc[((int64_t)bh * nqb + qb0) * D + i];
-  const __nv_bfloat16* base = kc + (int64_t)bh * nkb * D + d;
+  __shared__ __align__(16) __nv_bfloat16 s_kc[kRingStages][kRingRows][D];
+  const __nv_bfloat16* kc_bh = kc + (int64_t)bh * nkb * D;
   // The batch's own key blocks in a ragged launch (kc rows past them are padding).
   const int nb = tk_b ? min(max((tk_b[bh / H] + kBlock - 1) / kBlock, 1), nkb) : nkb;
+  const int nchunks = (nb + kRingRows - 1) / kRingRows;
+  // Rows [c * kRingRows, ...) of the head into stage c % kRingStages; one commit group per
+  // chunk (empty past the end) so that the wait below always counts the same groups.
+  auto issue = [&](int c) {
+    if (c < nchunks) {
+      for (int i = d; i < kRingRows * (D / 8); i += D) {
+        const int r = i / (D / 8), col = 8 * (i % (D / 8));
+        const int row = c * kRingRows + r;
+        if (row < nb)
+          cp_async16(smem_u32(&s_kc[c % kRingStages][r][col]), kc_bh + (int64_t)row * D + col, 16);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int c = 0; c < kRingStages - 1; ++c) issue(c);
   float s1 = 0.f, s2 = 0.f;
-  for (int j = 0; j < nb; ++j) {
-    const float x = __bfloat162float(base[(int64_t)j * D]);
-    s1 = __fadd_rn(s1, x);
-    s2 = __fadd_rn(s2, __fmul_rn(x, x));
+  for (int c = 0; c < nchunks; ++c) {
+    cp_async_wait<kRingStages - 2>();  // this thread's copies of chunk c have landed
+    __syncthreads();  // everyone's have, and every thread is done with chunk c - 1's stage
+    issue(c + kRingStages - 1);  // into the stage chunk c - 1 used
+    const int rows = min(kRingRows, nb - c * kRingRows);
+    const __nv_bfloat16* col = &s_kc[c % kRingStages][0][d];
+    for (int r = 0; r < rows; ++r) {
+      const float x = __bfloat162float(col[r * D]);
+      s1 = __fadd_rn(s1, x);
+      s2 = __fadd_rn(s2, __fmul_rn(x, x));
+    }
   }
+  cp_async_wait<0>();
   const float n = (float)nb;
   const float mean = __fdiv_rn(s1, n);
   const float var = fmaxf(__fsub_rn(__fdiv_rn(s2, n), __fmul_rn(mean, mean)), 0.f);
