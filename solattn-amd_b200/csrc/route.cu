@@ -3,7 +3,8 @@
 // CTAs start on their tiles at once.
 //
 // One CTA per (b, h) and group of kRouteQB q-blocks, 256 threads.  A warp stages its 32
-// centroid rows in shared memory with coalesced 16-byte loads, then lane kb forms the proxies
+// centroid rows in shared memory with coalesced 16-byte cp.async copies (double-buffered: the
+// next 64 dims or the next 32 rows are in flight while these are used), then lane kb forms the proxies
 // of all the group's q-blocks from row kb,
 // with exactly the arithmetic of common.cuh:routing_dot (eight partial sums over d = 8i + j,
 // __fmul_rn / __fadd_rn, combined pairwise), so the decisions are bit-identical to the
@@ -21,6 +22,9 @@ namespace {
 
 constexpr int kRouteQB = 4;
 constexpr int kRouteThreads = 256;
+constexpr int kRowBytes = 144;                // staged centroid row (64 dims) + 16 bytes of skew
+constexpr int kStageBytes = 32 * kRowBytes;   // one warp's 32 rows
+constexpr int kRouteSmem = (kRouteThreads / 32) * 2 * kStageBytes;  // double-buffered, dynamic
 
 template <int D>
 __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParams p) {
@@ -47,15 +51,36 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
                             : 0.f;
   __syncthreads();
 
-  // Per-warp staging of its 32 centroid rows, 64 dims at a time: rows are 144 bytes apart so
-  // that the lanes' 16-byte reads of 32 different rows take the minimum 4 wavefronts.
-  constexpr int kRowBytes = 144;
-  __shared__ __align__(16) uint8_t stage[kRouteThreads / 32][32 * kRowBytes];
+  // Per-warp staging of its 32 centroid rows, 64 dims at a time, double-buffered: the 16-byte
+  // cp.async copies of the next chunk (next half, or next word) are in flight while this one is
+  // computed.  Rows are 144 bytes apart so that the lanes' 16-byte reads of 32 different rows
+  // take the minimum 4 wavefronts.
+  extern __shared__ __align__(16) uint8_t route_smem[];
   const __nv_bfloat16* kc_bh = p.kc + (int64_t)bh * p.nkb * D;
-  const int lane = threadIdx.x & 31;
-  uint8_t* my_stage = stage[threadIdx.x >> 5];
+  const int lane = threadIdx.x & 31, warp_id = threadIdx.x >> 5;
+  uint8_t* my_stage = route_smem + warp_id * 2 * kStageBytes;
+  constexpr int kHalves = D / 64;
+  // This warp's chunks: t = m * kHalves + half for its m-th word w = warp_id + 8 m.
+  const int my_words = nwords > warp_id ? (nwords - warp_id + 7) / 8 : 0;
+  const int nchunks = p.force == 0 ? my_words * kHalves : 0;
+  auto issue = [&](int t) {
+    if (t < nchunks) {
+      const int w = warp_id + (kRouteThreads / 32) * (t / kHalves), half = t % kHalves;
+      uint8_t* dst = my_stage + (t & 1) * kStageBytes;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {  // 8 consecutive lanes copy one row's 128 bytes
+        const int idx = 32 * u + lane, r = idx >> 3, c = idx & 7;
+        const int kr = min(32 * w + r, nkb_b - 1);  // clamped: every address stays in range
+        cp_async16(smem_u32(dst + r * kRowBytes + 16 * c), kc_bh + (int64_t)kr * D + 64 * half + 8 * c,
+                   16);
+      }
+    }
+    cp_async_commit();
+  };
+  issue(0);
+  int t = 0;
   // Warp-uniform loop over 32-block words.
-  for (int w = threadIdx.x >> 5; w < nwords; w += kRouteThreads / 32) {
+  for (int w = warp_id; w < nwords; w += kRouteThreads / 32) {
     const int kb = 32 * w + lane;
     float part[kRouteQB][8];
 #pragma unroll
@@ -64,21 +89,15 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
       for (int e = 0; e < 8; ++e) part[j][e] = 0.f;
     if (p.force == 0) {
 #pragma unroll 1
-      for (int half = 0; half < D / 64; ++half) {
-        // Coalesced: 8 consecutive lanes read one row's 128 bytes of these 64 dims.
-        __syncwarp();
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int idx = 32 * t + lane, r = idx >> 3, c = idx & 7;
-          const int kr = min(32 * w + r, nkb_b - 1);  // clamped: every address stays in range
-          const uint4 v = __ldg(reinterpret_cast<const uint4*>(kc_bh + (int64_t)kr * D + 64 * half) + c);
-          *reinterpret_cast<uint4*>(my_stage + r * kRowBytes + 16 * c) = v;
-        }
-        __syncwarp();
+      for (int half = 0; half < kHalves; ++half, ++t) {
+        issue(t + 1);
+        cp_async_wait<1>();  // this lane's copies of chunk t have landed
+        __syncwarp();        // and every lane's
+        const uint8_t* cur = my_stage + (t & 1) * kStageBytes;
 #pragma unroll 4
       for (int ii = 0; ii < 8; ++ii) {
         const int i = 8 * half + ii;
-        const uint4 raw = *reinterpret_cast<const uint4*>(my_stage + lane * kRowBytes + 16 * ii);
+        const uint4 raw = *reinterpret_cast<const uint4*>(cur + lane * kRowBytes + 16 * ii);
         const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
         float kf[8];
 #pragma unroll
@@ -97,6 +116,7 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
           for (int e = 0; e < 8; ++e) part[j][e] = __fadd_rn(part[j][e], __fmul_rn(qv[e], kf[e]));
         }
       }
+        __syncwarp();  // every lane is done with this stage before chunk t + 2 overwrites it
       }
     }
 #pragma unroll
@@ -116,6 +136,7 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
       }
     }
   }
+  cp_async_wait<0>();  // (only empty groups can be pending here)
   if (!p.lists || nwords > kMaxWords) return;
   __syncthreads();
   // Warp j: the tile list of the group's q-block pair j (q-blocks qb_lo + 2j, qb_lo + 2j + 1).
@@ -140,10 +161,18 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
 
 cudaError_t launch_route(const AttnParams& p, int D, cudaStream_t stream) {
   dim3 grid((p.nqb + kRouteQB - 1) / kRouteQB, p.B * p.H);
-  if (D == 128)
-    route_kernel<128><<<grid, kRouteThreads, 0, stream>>>(p);
-  else
-    route_kernel<64><<<grid, kRouteThreads, 0, stream>>>(p);
+  cudaError_t err;
+  if (D == 128) {
+    err = cudaFuncSetAttribute(route_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kRouteSmem);
+    if (err != cudaSuccess) return err;
+    route_kernel<128><<<grid, kRouteThreads, kRouteSmem, stream>>>(p);
+  } else {
+    err = cudaFuncSetAttribute(route_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kRouteSmem);
+    if (err != cudaSuccess) return err;
+    route_kernel<64><<<grid, kRouteThreads, kRouteSmem, stream>>>(p);
+  }
   return cudaGetLastError();
 }
 
