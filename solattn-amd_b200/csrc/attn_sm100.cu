@@ -415,7 +415,7 @@ __device__ __forceinline__ bool item_epilogue(uint32_t tmem, uint32_t bar0, int 
 }  // namespace
 
 
-template <int D>
+template <int D, bool kLateClaim>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_sm100_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -497,12 +497,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // balances the CTAs' work up to the last items; claimed early, the last rounds of items
     // are handed out by the state of the CTAs two items before, which leaves a tail of about
     // one item (measured at 3 heads of the bench workload, 5 items per CTA: 7 % of the
-    // kernel's time; at 41 items per CTA the early claim is 0.7 % faster).
-    const bool early = total >= kEarlyClaimItems * (int)gridDim.x;
+    // kernel's time).  The two modes are two instantiations (kLateClaim), so that the early
+    // one is compiled from the same producer code as before the late mode existed: the kernel's
+    // speed at many items per CTA moved by several per cent with changes to producer code it
+    // does not even execute.
+    constexpr bool early = !kLateClaim;
     int item = (int)blockIdx.x;
     int next = item + (int)gridDim.x;
-    if (early && counter && lane == 0) next = (int)gridDim.x + (int)atomicAdd(counter, 1u);
-    next = __shfl_sync(0xffffffffu, next, 0);
+    if constexpr (early) {
+      if (counter && lane == 0) next = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+      next = __shfl_sync(0xffffffffu, next, 0);
+    }
     MaskWords mw = load_mask_words(p, item, total, nwords, lane);
     int g = 0;  // tiles of this CTA's earlier items
     int k_issued = 0, v_issued = 0, q_issued = 0;
@@ -540,7 +545,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++q_issued;
       // Early claim: the item after next, used two items on.
       int next2 = next + (int)gridDim.x;
-      if (early && counter && lane == 0) next2 = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+      if constexpr (early) {
+        if (counter && lane == 0) next2 = (int)gridDim.x + (int)atomicAdd(counter, 1u);
+      }
       // The tile list, once the item two back has released the buffer.
       if (k >= 2 && !warp_wait(bar(LIST_EMPTY + lb), (uint32_t)((k >> 1) - 1) & 1u, abort_flag,
                                p.status)) {
@@ -568,34 +575,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(bar(LIST_FULL + lb));
         }
       }
-      if (early) mw = load_mask_words(p, next, total, nwords, lane);
+      if constexpr (early) mw = load_mask_words(p, next, total, nwords, lane);
       // The producer reads the list too (its K/V loads follow the entries).
       if (p.lists && !warp_wait(bar(LIST_FULL + lb), (uint32_t)(k >> 1) & 1u, abort_flag, p.status)) {
         ok = false;
         break;
       }
-      // Late claim of the next item: lane 0 issues the atomicAdd before tile claim_at and goes
-      // on issuing tiles; two tiles later, when the result has returned, the warp reads it and
-      // loads the item's mask words.
-      const int claim_at = max(0, ntiles - kClaimTiles);
-      const int read_at = min(ntiles, claim_at + 2);
-      int claimed = item + (int)gridDim.x;
-      auto claim_issue = [&]() {
-        if (!early && counter && lane == 0) claimed = (int)gridDim.x + (int)atomicAdd(counter, 1u);
-      };
-      auto claim_read = [&]() {
-        if (early) return;
-        next = __shfl_sync(0xffffffffu, claimed, 0);
-        mw = load_mask_words(p, next, total, nwords, lane);
-      };
-      // K and V tiles of the item
-      if (!p.k.idx) {
-        const int bounds[4] = {0, claim_at, read_at, ntiles};
-        for (int phase = 0; phase < 3 && ok; ++phase) {
-          if (phase == 1) claim_issue();
-          if (phase == 2) claim_read();
+      if constexpr (early) {
+        // K and V tiles of the item
+        if (!p.k.idx) {
           if (lane == 0) {
-            for (int i = bounds[phase]; i < bounds[phase + 1]; ++i) {
+            for (int i = 0; i < ntiles; ++i) {
               const int gi = g + i, s = gi % kStages;
               const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;  // parity of the last use
               if (gi >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
@@ -613,56 +603,135 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
+        } else {
+          // Gathered K/V rows: the whole warp copies; a tile's 64 row indices (shared by K and
+          // V) are loaded one tile ahead.  Centroid tiles still come by TMA (lane 0), the other
+          // lanes arriving on the barrier, which counts one arrival per lane in this mode.
+          const int64_t* kvidx = p.k.idx + (int64_t)ip.b * p.Tk;
+          auto row_idx = [&](int e) {
+            RowIdx<kKeys> ri;
+            if (e >= 0) {
+              ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, tk - e * kBlock, lane,
+                                       p.status);
+            } else {
+              ri.t[0] = ri.t[1] = 0;
+            }
+            return ri;
+          };
+          RowIdx<kKeys> ri = row_idx(ntiles > 0 ? tl[0] : -1);
+          for (int i = 0; i < ntiles; ++i) {
+            const int gi = g + i, s = gi % kStages;
+            const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;
+            const int e = tl[i];
+            if (gi >= kStages && !warp_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            if (e >= 0) gather_tile<D, kKeys>(sK + s * L::kKVTile, kKVBox, p.k, ri, ip.h, lane, bar(K_FULL + s));
+            else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, ip.h, ip.b);
+            else mbar_arrive(bar(K_FULL + s));
+            ++k_issued;
+            if (gi >= kStages && !warp_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            if (e >= 0) gather_tile<D, kKeys>(sV + s * L::kKVTile, kKVBox, p.v, ri, ip.h, lane, bar(V_FULL + s));
+            else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, ip.h, ip.b);
+            else mbar_arrive(bar(V_FULL + s));
+            ++v_issued;
+            if (i + 1 < ntiles) ri = row_idx(tl[i + 1]);
+          }
         }
       } else {
-        // Gathered K/V rows: the whole warp copies; a tile's 64 row indices (shared by K and
-        // V) are loaded one tile ahead.  Centroid tiles still come by TMA (lane 0), the other
-        // lanes arriving on the barrier, which counts one arrival per lane in this mode.
-        const int64_t* kvidx = p.k.idx + (int64_t)ip.b * p.Tk;
-        auto row_idx = [&](int e) {
-          RowIdx<kKeys> ri;
-          if (e >= 0) {
-            ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, tk - e * kBlock, lane,
-                                     p.status);
-          } else {
-            ri.t[0] = ri.t[1] = 0;
-          }
-          return ri;
+        // Late claim of the next item: lane 0 issues the atomicAdd before tile claim_at and goes
+        // on issuing tiles; two tiles later, when the result has returned, the warp reads it and
+        // loads the item's mask words.
+        const int claim_at = max(0, ntiles - kClaimTiles);
+        const int read_at = min(ntiles, claim_at + 2);
+        int claimed = item + (int)gridDim.x;
+        auto claim_issue = [&]() {
+          if (counter && lane == 0) claimed = (int)gridDim.x + (int)atomicAdd(counter, 1u);
         };
-        RowIdx<kKeys> ri = row_idx(ntiles > 0 ? tl[0] : -1);
-        for (int i = 0; i < ntiles; ++i) {
-          if (i == claim_at) claim_issue();
-          if (i == read_at) claim_read();
-          const int gi = g + i, s = gi % kStages;
-          const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;
-          const int e = tl[i];
-          if (gi >= kStages && !warp_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
-            ok = false;
-            break;
+        auto claim_read = [&]() {
+          next = __shfl_sync(0xffffffffu, claimed, 0);
+          mw = load_mask_words(p, next, total, nwords, lane);
+        };
+        // K and V tiles of the item
+        if (!p.k.idx) {
+          const int bounds[4] = {0, claim_at, read_at, ntiles};
+          for (int phase = 0; phase < 3 && ok; ++phase) {
+            if (phase == 1) claim_issue();
+            if (phase == 2) claim_read();
+            if (lane == 0) {
+              for (int i = bounds[phase]; i < bounds[phase + 1]; ++i) {
+                const int gi = g + i, s = gi % kStages;
+                const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;  // parity of the last use
+                if (gi >= kStages && !mbar_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
+                  ok = false;
+                  break;
+                }
+                load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), tl[i], ip.h, ip.b);
+                ++k_issued;
+                if (gi >= kStages && !mbar_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
+                  ok = false;
+                  break;
+                }
+                load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), tl[i], ip.h, ip.b);
+                ++v_issued;
+              }
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
           }
-          if (e >= 0) gather_tile<D, kKeys>(sK + s * L::kKVTile, kKVBox, p.k, ri, ip.h, lane, bar(K_FULL + s));
-          else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, ip.h, ip.b);
-          else mbar_arrive(bar(K_FULL + s));
-          ++k_issued;
-          if (gi >= kStages && !warp_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
-            ok = false;
-            break;
+        } else {
+          // Gathered K/V rows: the whole warp copies; a tile's 64 row indices (shared by K and
+          // V) are loaded one tile ahead.  Centroid tiles still come by TMA (lane 0), the other
+          // lanes arriving on the barrier, which counts one arrival per lane in this mode.
+          const int64_t* kvidx = p.k.idx + (int64_t)ip.b * p.Tk;
+          auto row_idx = [&](int e) {
+            RowIdx<kKeys> ri;
+            if (e >= 0) {
+              ri = load_row_idx<kKeys>(p.k, kvidx + (int64_t)e * kBlock, tk - e * kBlock, lane,
+                                       p.status);
+            } else {
+              ri.t[0] = ri.t[1] = 0;
+            }
+            return ri;
+          };
+          RowIdx<kKeys> ri = row_idx(ntiles > 0 ? tl[0] : -1);
+          for (int i = 0; i < ntiles; ++i) {
+            if (i == claim_at) claim_issue();
+            if (i == read_at) claim_read();
+            const int gi = g + i, s = gi % kStages;
+            const uint32_t prev = (uint32_t)(gi / kStages - 1) & 1u;
+            const int e = tl[i];
+            if (gi >= kStages && !warp_wait(bar(K_EMPTY + s), prev, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            if (e >= 0) gather_tile<D, kKeys>(sK + s * L::kKVTile, kKVBox, p.k, ri, ip.h, lane, bar(K_FULL + s));
+            else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sK + s * L::kKVTile, &tmK, &tmKC, bar(K_FULL + s), e, ip.h, ip.b);
+            else mbar_arrive(bar(K_FULL + s));
+            ++k_issued;
+            if (gi >= kStages && !warp_wait(bar(PV_DONE + s), prev, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            if (e >= 0) gather_tile<D, kKeys>(sV + s * L::kKVTile, kKVBox, p.v, ri, ip.h, lane, bar(V_FULL + s));
+            else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, ip.h, ip.b);
+            else mbar_arrive(bar(V_FULL + s));
+            ++v_issued;
+            if (i + 1 < ntiles) ri = row_idx(tl[i + 1]);
           }
-          if (e >= 0) gather_tile<D, kKeys>(sV + s * L::kKVTile, kKVBox, p.v, ri, ip.h, lane, bar(V_FULL + s));
-          else if (lane == 0 || e == kDummyTile) load_kv_tile<D>(sV + s * L::kKVTile, &tmV, &tmVC, bar(V_FULL + s), e, ip.h, ip.b);
-          else mbar_arrive(bar(V_FULL + s));
-          ++v_issued;
-          if (i + 1 < ntiles) ri = row_idx(tl[i + 1]);
+          if (ok && read_at == ntiles) {  // fewer than three tiles after claim_at
+            if (claim_at == ntiles) claim_issue();
+            claim_read();
+          }
         }
-        if (ok && read_at == ntiles) {  // fewer than three tiles after claim_at
-          if (claim_at == ntiles) claim_issue();
-          claim_read();
-        }
+        if (!ok) break;
       }
-      if (!ok) break;
       g += ntiles;
       item = next;
-      if (early) next = __shfl_sync(0xffffffffu, next2, 0);
+      if constexpr (early) next = __shfl_sync(0xffffffffu, next2, 0);
     }
     if (p.q.idx || p.k.idx) cp_async_wait_all();  // no copy may still write shared memory
     if (lane == 0 && *abort_flag) {
@@ -1079,9 +1148,6 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
   }
   const size_t smem = Layout<D>::bytes(p.nkb);
-  err = cudaFuncSetAttribute(attn_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-  if (err != cudaSuccess) return err;
   // Persistent grid: one CTA per SM, each working through items until none are left.
   const int64_t items = (int64_t)((p.nqb + 1) / 2) * p.B * p.H;
   if (items > 0x7fff0000) return cudaErrorInvalidValue;
@@ -1090,7 +1156,12 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
   if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (err != cudaSuccess) return err;
   const int64_t ctas = items < sms ? items : sms;
-  attn_sm100_kernel<D><<<(unsigned)ctas, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
+  // Fewer than kEarlyClaimItems items per CTA: the instantiation that claims items late.
+  auto* kernel = items < (int64_t)kEarlyClaimItems * ctas ? attn_sm100_kernel<D, true>
+                                                          : attn_sm100_kernel<D, false>;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  kernel<<<(unsigned)ctas, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
   return cudaGetLastError();
 }
 
