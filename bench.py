@@ -55,7 +55,7 @@ def peaks():
 def ncu_traffic(heads):
     """DRAM bytes (read + write) of one attention launch over `heads` heads, from the committed
     ncu summary of the full 24-head launch (traffic scales with the head count), if present."""
-    f = ROOT / "profiles" / "attn_sm100_video_dit_t32k_h8.md"
+    f = ROOT / "profiles" / "attn_sm100_video_dit_t32k_h12.md"
     try:
         for line in f.read_text().splitlines():
             if line.startswith("attention_bytes_per_launch="):
