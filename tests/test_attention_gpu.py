@@ -165,3 +165,16 @@ def test_sol_matches_oracle_on_random_shapes():
         assert_close(actual.cpu(), ref)
         assert_north_star(actual.cpu(), ref)
         assert (stats.exact_blocks.cpu() - counts).abs().sum() <= 2
+
+
+def test_claim_modes_give_identical_results():
+    """The fused kernel claims work items early (item after next, at 16 or more items per CTA)
+    or late (while the current item's last tiles load).  Results do not depend on which CTA ran
+    an item: a 40-head call (2560 items, early) and a 4-head call on the same tensors (256
+    items, late) must agree bit for bit on those heads, counts included."""
+    q, k, v = (to_device(x) for x in workloads.video_dit(t=8192, h=40, d=128, sigma=0.3, seed=3))
+    kw = dict(beta=1.0, kv_sink_tokens=128, query_sink_tokens=128, local_blocks=1)
+    full, full_stats = sol_attention(q, k, v, return_stats=True, **kw)
+    part, part_stats = sol_attention(q[:, :, 4:8], k[:, :, 4:8], v[:, :, 4:8], return_stats=True, **kw)
+    assert torch.equal(part, full[:, :, 4:8])
+    assert torch.equal(part_stats.exact_blocks, full_stats.exact_blocks[:, :, 4:8])
