@@ -14,7 +14,7 @@
 // list buffer is given the pass also builds every q-block pair's tile list for the fused kernel
 // (common.cuh: build_item_list) and writes the exact-block counts, so that no attention CTA
 // spends time on either between two items.
-#include "common.cuh"
+#include "sm100.cuh"
 
 namespace solattn {
 
@@ -82,11 +82,14 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   // Warp-uniform loop over 32-block words.
   for (int w = warp_id; w < nwords; w += kRouteThreads / 32) {
     const int kb = 32 * w + lane;
-    float part[kRouteQB][8];
+    // Partial sums of dims 8i + e in pairs (e, e + 1) of packed f32x2 registers: each lane of
+    // mul.rn.f32x2 / add.rn.f32x2 rounds exactly like __fmul_rn / __fadd_rn (no contraction),
+    // so the sums are those of the scalar order with half the instructions.
+    uint64_t part2[kRouteQB][4];
 #pragma unroll
     for (int j = 0; j < kRouteQB; ++j)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) part[j][e] = 0.f;
+      for (int e = 0; e < 4; ++e) part2[j][e] = 0ull;
     if (p.force == 0) {
 #pragma unroll 1
       for (int half = 0; half < kHalves; ++half, ++t) {
@@ -99,21 +102,21 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
         const int i = 8 * half + ii;
         const uint4 raw = *reinterpret_cast<const uint4*>(cur + lane * kRowBytes + 16 * ii);
         const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-        float kf[8];
+        uint64_t kf2[4];  // dims (8i + 2e, 8i + 2e + 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __bfloat1622float2(k2[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
+          kf2[e] = sm100::f2_pack(f.x, f.y);
         }
 #pragma unroll
         for (int j = 0; j < kRouteQB; ++j) {
-          // The q-block means of dims 8i..8i+7: two 16-byte broadcast reads.
-          const float4 qa = *reinterpret_cast<const float4*>(&sq[j][8 * i]);
-          const float4 qb4 = *reinterpret_cast<const float4*>(&sq[j][8 * i + 4]);
-          const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb4.x, qb4.y, qb4.z, qb4.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) part[j][e] = __fadd_rn(part[j][e], __fmul_rn(qv[e], kf[e]));
+          // The q-block means of dims 8i..8i+7 as four packed pairs: two 16-byte broadcast reads.
+          const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(&sq[j][8 * i]);
+          const ulonglong2 qb4 = *reinterpret_cast<const ulonglong2*>(&sq[j][8 * i + 4]);
+          part2[j][0] = sm100::f2_add(part2[j][0], sm100::f2_mul(qa.x, kf2[0]));
+          part2[j][1] = sm100::f2_add(part2[j][1], sm100::f2_mul(qa.y, kf2[1]));
+          part2[j][2] = sm100::f2_add(part2[j][2], sm100::f2_mul(qb4.x, kf2[2]));
+          part2[j][3] = sm100::f2_add(part2[j][3], sm100::f2_mul(qb4.y, kf2[3]));
         }
       }
         __syncwarp();  // every lane is done with this stage before chunk t + 2 overwrites it
@@ -123,10 +126,13 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
     for (int j = 0; j < kRouteQB; ++j) {
       if (j >= nq) break;
       const int qb = qb_lo + j;
-      const float dot = __fadd_rn(__fadd_rn(__fadd_rn(part[j][0], part[j][1]),
-                                            __fadd_rn(part[j][2], part[j][3])),
-                                  __fadd_rn(__fadd_rn(part[j][4], part[j][5]),
-                                            __fadd_rn(part[j][6], part[j][7])));
+      float part[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sm100::f2_unpack(part2[j][e], part[2 * e], part[2 * e + 1]);
+      const float dot = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]),
+                                            __fadd_rn(part[2], part[3])),
+                                  __fadd_rn(__fadd_rn(part[4], part[5]),
+                                            __fadd_rn(part[6], part[7])));
       bool sel = false;
       if (kb < nkb_b) sel = route_rules(p, p.force == 0 && __fmul_rn(dot, p.scale) > scut[j], b, qb, kb);
       const uint32_t bal = __ballot_sync(0xffffffffu, sel);
