@@ -10,7 +10,7 @@
 //
 // The pass is HBM-bound: it reads every Q/K/V element once (the 64 rows of a unit are
 // strided by sT, each row a contiguous 2*D-byte segment) and writes 1/64 of that back.
-#include "common.cuh"
+#include "sm100.cuh"
 
 namespace solattn {
 
@@ -33,16 +33,20 @@ __global__ void __launch_bounds__(256) pool_kernel(PoolParams p) {
   }
   const bool active = which < 3;
   int b = 0, blk = 0, h = 0, n = 0;
-  float acc[8];
+  // Sums of channels (2j, 2j + 1) in packed f32x2 pairs: each lane of add.rn.f32x2 rounds like
+  // __fadd_rn, so the sums are those of the scalar order with half the adds.
+  uint64_t acc2[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int j = 0; j < 4; ++j) acc2[j] = 0ull;
   if (active) {
     const TensorView& x = p.x[which];
     const int T = p.T[which];
-    h = (int)(unit % p.H);
-    int64_t r = unit / p.H;
-    blk = (int)(r % p.nb[which]);
-    b = (int)(r / p.nb[which]);
+    // Unit indices fit 32 bits (the launcher checks), so the decode uses 32-bit division.
+    const int u32 = (int)unit;
+    h = u32 % p.H;
+    const int r = u32 / p.H;
+    blk = r % p.nb[which];
+    b = r / p.nb[which];
     const int Tv = (which > 0 && p.tk_b) ? clamp_key_count(__ldg(p.tk_b + b), T, p.status)
                                          : T;  // valid rows of this batch
     n = min(kBlock, Tv - blk * kBlock);
@@ -62,15 +66,15 @@ __global__ void __launch_bounds__(256) pool_kernel(PoolParams p) {
         const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float2 f = __bfloat1622float2(v2[j]);
-          acc[2 * j] = __fadd_rn(acc[2 * j], f.x);
-          acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], f.y);
+          const float2 f = __bfloat1622float2(v2[j]);
+          acc2[j] = sm100::f2_add(acc2[j], sm100::f2_pack(f.x, f.y));
         }
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) part[local_unit][g][c * 8 + i] = acc[i];
+  for (int j = 0; j < 4; ++j)
+    sm100::f2_unpack(acc2[j], part[local_unit][g][c * 8 + 2 * j], part[local_unit][g][c * 8 + 2 * j + 1]);
   __syncthreads();
   if (!active) return;
   // Thread lt now owns channel lt of the unit.
@@ -90,6 +94,8 @@ __global__ void __launch_bounds__(256) pool_kernel(PoolParams p) {
 cudaError_t launch_pool(const PoolParams& p, int D, cudaStream_t stream) {
   const int64_t total = p.units[0] + p.units[1] + p.units[2];
   if (total == 0) return cudaSuccess;
+  for (int i = 0; i < 3; ++i)
+    if (p.units[i] > 0x7fffffff) return cudaErrorInvalidValue;  // 32-bit unit decode
   const int per_cta = 256 / D;
   const int64_t grid = (total + per_cta - 1) / per_cta;
   if (D == 128)
