@@ -1,6 +1,6 @@
 """Benchmark of the SOL routed-attention hot path (pool -> threshold -> fused attention).
 
-Workload (BASELINE metric): video-DiT self-attention B=1, T=32768, H=24, D=128 BF16,
+Workload (the headline metric's configuration): video-DiT self-attention B=1, T=32768, H=24, D=128 BF16,
 block-smooth with drift (sigma=0.3), beta=1.0, kv/query sinks 128/128, local_blocks=1,
 seeded synthetic inputs (no captured activations exist here).  Heads are sharded across the
 N ranks (one process per GPU, torchrun); there is no collective on the hot path: NCCL only
