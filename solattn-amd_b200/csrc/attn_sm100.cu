@@ -497,10 +497,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // balances the CTAs' work up to the last items; claimed early, the last rounds of items
     // are handed out by the state of the CTAs two items before, which leaves a tail of about
     // one item (measured at 3 heads of the bench workload, 5 items per CTA: 7 % of the
-    // kernel's time).  The two modes are two instantiations (kLateClaim), so that the early
-    // one is compiled from the same producer code as before the late mode existed: the kernel's
-    // speed at many items per CTA moved by several per cent with changes to producer code it
-    // does not even execute.
+    // kernel's time).  The two modes are two instantiations (kLateClaim) and the early one
+    // carries none of the late-claim code: the kernel's speed at many items per CTA changed by
+    // several per cent with changes to producer code that it does not execute (code placement
+    // and register allocation follow the whole kernel).
     constexpr bool early = !kLateClaim;
     int item = (int)blockIdx.x;
     int next = item + (int)gridDim.x;
