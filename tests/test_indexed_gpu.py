@@ -131,3 +131,21 @@ def test_ragged_plan_equals_separate_window_plans():
             assert torch.equal(scat[rows[w].cuda()], o1[0]), (beta, w)
     d = stats.density()
     assert 0.0 < d <= 1.0
+
+
+def test_window_sharded_plan_equals_full_plan_windows():
+    """Window sharding across ranks (one process per GPU): the sub-plan of windows [2, 5) of a
+    ragged plan gives, bit for bit, the outputs and exact-block counts of those windows in a
+    call on the whole plan."""
+    from sol_attn_b200 import workloads
+    from sol_attn_b200.sharding import plan_windows
+    t = 8192
+    q, k, v = (to_device(x[0]) for x in workloads.video_dit(t=t, h=4, d=128, sigma=0.3, seed=7))
+    wins = workloads.indexed_windows(t, window=512, halo=1024, anchor=256, stride=8)
+    plan = IndexedPlan.create(torch.stack([r for r, _ in wins]), [kk for _, kk in wins], t,
+                              protected_ranges=((0, 256),))
+    full, full_stats = sol_attention_indexed(q, k, v, plan.to("cuda"), beta=1.0, return_stats=True)
+    part, part_stats = sol_attention_indexed(q, k, v, plan_windows(plan, 2, 5).to("cuda"), beta=1.0,
+                                             return_stats=True)
+    assert torch.equal(part, full[2:5])
+    assert torch.equal(part_stats.exact_blocks, full_stats.exact_blocks[2:5])
