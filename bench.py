@@ -115,52 +115,52 @@ def make_inputs():
     return workloads.video_dit(b=B, t=T, h=H, d=D, sigma=0.3, seed=0)
 
 
-def time_cpu_oracle(qh, kh, vh, n_qblocks, threads, heads=(0,)):
-    """Oracle port on ``heads`` and ``n_qblocks`` evenly spaced q-blocks of each; the time is
-    extrapolated linearly to the whole call (all heads, all q-blocks).
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    Returns (seconds per full call, sample description, (blocks, output, counts) of head 0)."""
+
+def oracle_heads(qh, kh, vh, heads, threads):
+    """The CPU oracle port on whole heads (every q-block).  Returns (seconds per head, list of
+    (head, output [1, T, 1, D], counts [1, nqb, 1]))."""
     from oracle.sol_oracle import sol_oracle
     torch.set_num_threads(threads)
-    nqb = (T + 63) // 64
-    blocks = sorted(set(int(i * nqb / n_qblocks) for i in range(n_qblocks)))
     kw = dict(beta=BETA, local_blocks=LOCAL, kv_sink_tokens=SINK, query_sink_tokens=SINK)
-    t_head = t_blocks = 0.0
-    first = None
+    results, total = [], 0.0
     for h in heads:
         q1, k1, v1 = (x[:, :, h:h + 1].contiguous() for x in (qh, kh, vh))
         t0 = time.perf_counter()
-        sol_oracle(q1, k1, v1, query_blocks=[], **kw)  # pooling + moments + cutoffs of one head
-        t1 = time.perf_counter()
-        out, counts = sol_oracle(q1, k1, v1, query_blocks=blocks, **kw)
-        t2 = time.perf_counter()
-        t_head += t1 - t0
-        t_blocks += (t2 - t1) - (t1 - t0)
-        if first is None:
-            first = (blocks, out, counts)
-    per_head = t_head / len(heads)
-    per_block = max(t_blocks, 0.0) / (len(heads) * len(blocks))
-    per_call = H * per_head + H * nqb * per_block
-    sample = (f"heads {list(heads)}, {len(blocks)} of {nqb} q-blocks each (+ pooling of those "
-              f"heads), extrapolated linearly to {H} heads x {nqb} q-blocks")
-    return per_call, sample, first
+        out, counts = sol_oracle(q1, k1, v1, **kw)
+        total += time.perf_counter() - t0
+        results.append((h, out, counts))
+    return total / len(heads), results
 
 
 def reference_arm(args, rank, world):
+    """The reference's CPU path (the oracle port of its FP32 Torch oracle) on the host cores.
+    Each step is one measured sample: one whole head of the workload (pooling, moments, the
+    Eq. 15 cutoffs and all 512 q-blocks), so ``ms_per_step`` is what was timed and ``value`` is
+    that sample's dense-equivalent FLOPs over its time.  Only rank 0 works."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     qh, kh, vh = make_inputs()
-    n_qb = 128
-    for _ in range(args.warmup):
-        time_cpu_oracle(qh, kh, vh, 8, threads)
-    calls = []
-    sample = ""
-    for _ in range(args.steps):
-        per_call, sample, _ = time_cpu_oracle(qh, kh, vh, n_qb, threads)
-        calls.append(per_call)
-    ms = statistics.mean(calls) * 1e3
-    value = DENSE_FLOPS / (ms * 1e-3) / 1e12
+    sample_flops = DENSE_FLOPS / H
+    for i in range(args.warmup):
+        oracle_heads(qh, kh, vh, (i % H,), threads)
+    secs = []
+    for i in range(args.steps):
+        per_head, _ = oracle_heads(qh, kh, vh, ((args.warmup + i) % H,), threads)
+        secs.append(per_head)
+    ms = statistics.mean(secs) * 1e3
+    value = sample_flops / (ms * 1e-3) / 1e12
+    sample = (f"one whole head per step (head index = step mod {H}: pooling, moments, cutoffs "
+              f"and all {T // 64} q-blocks), {sample_flops / 1e12:.4f} dense-equivalent TFLOP")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -168,9 +168,56 @@ def reference_arm(args, rank, world):
             "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "heads": H,
                        "head_dim": D, "parallelism": "host CPU, oracle port"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": sample},
+                             "cpu_model": cpu_model(), "sample": sample,
+                             "extrapolated_call_s": statistics.mean(secs) * H},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def c5_leg(args, rank, world, dev, barrier):
+    """The indexed-window configuration: NHD [32768, 24, 128] (block-smooth drift, sigma 0.3),
+    64 windows of 512 queries, keys = anchor [0, 256) + own window +-1024 + every 8th key, one
+    ragged IndexedPlan (six key counts) sharded by windows across the ranks.  Plan creation and
+    transfer are timed apart from the calls."""
+    from sol_attn_b200 import IndexedPlan, sol_attention_indexed, workloads
+    from sol_attn_b200.sharding import max_over_ranks, plan_windows, window_shard
+    qh, kh, vh = make_inputs()
+    q, k, v = (x[0].to(dev) for x in (qh, kh, vh))
+    wins = workloads.indexed_windows(T, window=512, halo=1024, anchor=256, stride=8)
+    rows = torch.stack([r for r, _ in wins])
+    keys = [kk for _, kk in wins]
+    t0 = time.perf_counter()
+    plan = IndexedPlan.create(rows, keys, T, protected_ranges=((0, 256),))
+    t1 = time.perf_counter()
+    w0, w1 = window_shard(len(wins), rank, world)
+    mine = plan_windows(plan, w0, w1)
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    mine = mine.to(dev)
+    torch.cuda.synchronize()
+    t3 = time.perf_counter()
+    for _ in range(args.warmup):
+        sol_attention_indexed(q, k, v, mine, beta=BETA)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    for s_, e_ in ev:
+        flush.zero_()
+        s_.record()
+        sol_attention_indexed(q, k, v, mine, beta=BETA)
+        e_.record()
+    barrier()
+    ms = statistics.mean(s_.elapsed_time(e_) for s_, e_ in ev)
+    ms, = max_over_ranks([ms], device=dev)
+    flops = 4.0 * H * D * sum(r.numel() * kk.numel() for r, kk in wins)
+    return {"workload": "indexed windows: NHD [32768, 24, 128] bf16 (block-smooth drift sigma 0.3), "
+                        "64 windows x 512 queries, keys = [0, 256) + window +-1024 + every 8th, "
+                        "one ragged IndexedPlan, beta 1.0, window-sharded",
+            "windows_per_rank": f"{w1 - w0} (rank {rank})", "ms_per_call": ms,
+            "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "dense_equiv_tflop": flops / 1e12,
+            "plan_create_ms": (t1 - t0) * 1e3, "plan_transfer_ms": (t3 - t2) * 1e3,
+            "l2": "flushed between timed calls (256 MiB write)"}
 
 
 def main():
@@ -181,6 +228,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-c5", action="store_true", help="skip the indexed-window leg")
     ap.add_argument("--heads", type=int, default=H,
                     help="profiling only: run the first HEADS heads of the workload")
     args = ap.parse_args()
@@ -289,6 +337,9 @@ def main():
         h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
         d2h = hout.numel() * hout.element_size()
 
+    # ---------------- the indexed-window configuration (window-sharded) ----------------
+    c5 = None if args.no_c5 else c5_leg(args, rank, world, dev, barrier)
+
     # ---------------- reduce over ranks (after timing) ----------------
     from sol_attn_b200.sharding import gather_heads, max_over_ranks
     ms, e2e_ms, pool_ms, thr_ms, attn_ms = max_over_ranks(
@@ -311,23 +362,35 @@ def main():
 
     result = None
     if rank == 0:
-        err = None
+        # Parity of this run against the CPU oracle port on whole heads (every q-block):
+        # outputs within the north-star gate and exact-block counts compared one by one.
+        threads = os.cpu_count() or 1
+        check_heads = (0, 8, 16) if (world == 1 and h1 - h0 == H) else tuple(range(h0, min(h1, h0 + 3)))
+        per_head, refs = oracle_heads(qh, kh, vh, check_heads, threads)
+        dsum = rsum = d2 = r2 = 0.0
+        dmax = 0.0
+        mismatch = compared = 0
+        for h, ref, cref in refs:
+            got = st.out[:, :, h - h0:h - h0 + 1].float().cpu()
+            delta = (got - ref).abs()
+            dmax = max(dmax, float(delta.max()))
+            dsum += float(delta.sum())
+            rsum += float(ref.abs().sum())
+            d2 += float(((got - ref) ** 2).sum())
+            r2 += float((ref ** 2).sum())
+            gc = counts_all[:, :, h:h + 1].cpu()
+            mismatch += int((gc != cref).sum())
+            compared += gc.numel()
+        err = {"max_abs": dmax, "mean_rel": dsum / rsum, "rel_l2": (d2 / r2) ** 0.5,
+               "vs": "CPU oracle port, whole heads", "heads": list(check_heads),
+               "q_blocks": T // 64, "count_mismatches": mismatch, "counts_compared": compared}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            threads = os.cpu_count() or 1
-            per_call, sample, (blocks, ref, _) = time_cpu_oracle(qh, kh, vh, 512, threads,
-                                                                 heads=(0, 8, 16))
-            cpu = {"value": DENSE_FLOPS / per_call / 1e12, "unit": UNIT, "cores": threads,
-                   "kind": "port", "sample": sample, "seconds_per_call": per_call}
-        else:
-            _, _, (blocks, ref, _) = time_cpu_oracle(qh, kh, vh, 4, os.cpu_count() or 1)
-        got = st.out[:, :, 0:1].float().cpu()
-        rows = torch.cat([torch.arange(b * 64, b * 64 + 64) for b in blocks])
-        delta = (got[:, rows] - ref[:, rows]).abs()
-        err = {"max_abs": float(delta.max()),
-               "mean_rel": float(delta.sum() / ref[:, rows].abs().sum()),
-               "rel_l2": float((got[:, rows] - ref[:, rows]).norm() / ref[:, rows].norm()),
-               "vs": "CPU oracle, head 0, sampled q-blocks", "q_blocks": len(blocks)}
+            cpu = {"value": (DENSE_FLOPS / H) / per_head / 1e12, "unit": UNIT, "cores": threads,
+                   "kind": "port", "cpu_model": cpu_model(),
+                   "sample": f"heads {list(check_heads)} whole (pooling, moments, cutoffs, all "
+                             f"{T // 64} q-blocks each), timed head by head",
+                   "seconds_per_head": per_head, "extrapolated_call_s": per_head * H}
         result = {
             "metric": METRIC, "value": dense_flops / (ms * 1e-3) / 1e12, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -353,6 +416,7 @@ def main():
                        "copies overlapped with compute)",
                 "ms_per_call": e2e_ms, "h2d_bytes_per_step": h2d * world,
                 "d2h_bytes_per_step": d2h * world},
+            "c5": c5,
             "gpu_launches": st.launches() * args.steps * world,
             "clocks": clk.summary(),
         }

@@ -4,13 +4,15 @@
  *
  * Every entry point takes raw device pointers, sizes, element strides, scalars and a
  * CUDA stream passed as `void*` (a cudaStream_t; NULL is the legacy default stream). No
- * entry point allocates or synchronises (solattn_read_status excepted): buffers are owned by
+ * entry point allocates or synchronises (solattn_read_status and solattn_noalloc_read_status
+ * excepted): buffers are owned by
  * the caller (in the Python layer, torch), and only solattn_sol_forward_noalloc keeps state
  * between calls (its fixed scratch array). Work is enqueued on `stream` asynchronously.
  * Return value: SOLATTN_OK (0) or a negative SOLATTN_ERR_* code; solattn_strerror() gives
  * the message. Errors that a kernel detects on the device (a bounded wait that ran out, an
  * index outside its tensor) are written to the caller's status word (see
- * solattn_workspace_layout) and read with solattn_read_status().
+ * solattn_workspace_layout) and copied out with solattn_status_to_host() (asynchronous) or
+ * solattn_read_status() (blocking).
  *
  * Tensor conventions (mirroring zihaomu/SolAttn-AMD):
  *   - BTHD activations q [B, Tq, H, D], k and v [B, Tk, H, D], BF16, any positive element
@@ -200,23 +202,27 @@ SOLATTN_API int solattn_sol_forward_ex(const void* q, const void* k, const void*
  * v and out NHD [N, H, D] BF16 (element strides q_sT/q_sH etc.; the head dimension is
  * contiguous).  The VDN adapter's dense global-query step (`out[rows] = dense(q[rows], k, v)`,
  * integrations/vdn.py:58-63) without the gathered copy of Q or the scatter.  Needs no workspace.
+ * A row index outside [0, N) is skipped and reported through `status` (a device int32 word the
+ * caller clears, or NULL).
  */
 SOLATTN_API int solattn_dense_rows(const void* q, const void* k, const void* v,
                   const int64_t* rows, int64_t n_rows, int64_t N, int64_t H, int64_t D,
                   int64_t q_sT, int64_t q_sH, int64_t k_sT, int64_t k_sH,
-                  int64_t v_sT, int64_t v_sH, float scale, void* out, void* stream);
+                  int64_t v_sT, int64_t v_sH, float scale, void* out, int32_t* status,
+                  void* stream);
 
 /*
  * Dense noncausal attention over all keys (BF16 QK/PV, FP32 softmax).  Replaces
  * `launch_dense`/`_dense` (kernels.py:67-98, 193-200); implemented as the all-exact route
- * of the fused kernel, so it needs no workspace.
+ * of the fused kernel, so it needs no workspace.  `status`: a device int32 word that receives
+ * device-side errors (a bounded wait that ran out), cleared by the caller, or NULL.
  */
 SOLATTN_API int solattn_dense(const void* q, const void* k, const void* v,
                   int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
                   int64_t q_sB, int64_t q_sT, int64_t q_sH,
                   int64_t k_sB, int64_t k_sT, int64_t k_sH,
                   int64_t v_sB, int64_t v_sT, int64_t v_sH,
-                  float scale, void* out, void* stream);
+                  float scale, void* out, int32_t* status, void* stream);
 
 /*
  * All-in SOL forward that allocates nothing (no counterpart in the reference).
@@ -248,6 +254,15 @@ SOLATTN_API int solattn_sol_forward_noalloc(const void* q, const void* k, const 
  * in the reference). */
 SOLATTN_API int64_t solattn_noalloc_scratch_bytes(void);
 
+/* Device address of that scratch array on the current device (no counterpart in the reference).
+ * Its first int32 is the status word of the last solattn_sol_forward_noalloc call on the device:
+ * pass it to solattn_status_to_host for a check that does not block. */
+SOLATTN_API int solattn_noalloc_scratch_address(void** address);
+
+/* solattn_read_status on the no-allocation status word of the current device (no counterpart in
+ * the reference): synchronises `stream`, returns the word through *value and clears it. */
+SOLATTN_API int solattn_noalloc_read_status(int32_t* value, void* stream);
+
 /*
  * Strided 2-D copy between host and device memory on `stream` (no counterpart in the reference,
  * whose API takes device tensors only): `rows` rows of `width_bytes` bytes, consecutive rows
@@ -261,8 +276,21 @@ SOLATTN_API int solattn_copy_2d(void* dst, int64_t dst_pitch, const void* src, i
                                 int64_t width_bytes, int64_t rows, int direction, void* stream);
 
 /*
+ * Enqueues on `stream` an asynchronous copy of the device status word at `status` into
+ * `host_dst` (pinned host memory for the copy to stay asynchronous) and returns at once.  The
+ * word is final once the stream has passed the copy (an event recorded after it has
+ * completed); nonzero = a kernel of the calls enqueued before reported a device-side error
+ * (1 a bounded wait ran out, 2 an index outside its tensor, 3 TMEM, 4 a TMA coordinate).
+ * The Python layer copies every call's status this way and raises on the next call (or on
+ * SolStats.density()), so production calls never block on it.  No counterpart in the
+ * reference, whose kernels report nothing.
+ */
+SOLATTN_API int solattn_status_to_host(const int32_t* status, int32_t* host_dst, void* stream);
+
+/*
  * Synchronises `stream`, copies the device status word at `status` to the host, clears it
- * and returns it through *value (0 = no device-side error).  Diagnostic use only: it blocks.
+ * and returns it through *value (0 = no device-side error).  It blocks: the non-blocking form
+ * is solattn_status_to_host.
  */
 SOLATTN_API int solattn_read_status(int32_t* status, int32_t* value, void* stream);
 

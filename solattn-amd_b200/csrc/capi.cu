@@ -1,6 +1,6 @@
 // extern "C" entry points of libsolattn.so (declared in include/solattn.h).
 // Argument checking here is the C-side contract; the Python layer performs the reference's
-// ValueError validation (attention.py:25-45) before it gets this far.
+// ValueError validation (attention.py:19-44) before it gets this far.
 #include <math.h>
 #include <stdio.h>
 
@@ -32,6 +32,10 @@ bool strides_ok(int64_t sB, int64_t sT, int64_t sH) {
   return sB >= 0 && sT > 0 && sH > 0 && sB % 8 == 0 && sT % 8 == 0 && sH % 8 == 0;
 }
 
+}  // namespace
+
+// Shape contract shared by every entry point (also used by noalloc.cu).
+namespace solattn {
 int check_shapes(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   if (B <= 0 || Tq <= 0 || Tk <= 0 || H <= 0) return SOLATTN_ERR_ARG;
   if (D != 64 && D != 128) return SOLATTN_ERR_UNSUPPORTED;
@@ -40,6 +44,9 @@ int check_shapes(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   if (cdiv(Tq, kBlock) > 65535 * 64 || B * H > 65535) return SOLATTN_ERR_UNSUPPORTED;
   return SOLATTN_OK;
 }
+}  // namespace solattn
+
+namespace {
 
 TensorView view(const void* ptr, int64_t sB, int64_t sT, int64_t sH, const int64_t* idx,
                 int64_t rows) {
@@ -388,25 +395,25 @@ int solattn_sol_forward_ex(const void* q, const void* k, const void* v, int64_t 
 int solattn_dense_rows(const void* q, const void* k, const void* v, const int64_t* rows,
                        int64_t n_rows, int64_t N, int64_t H, int64_t D, int64_t q_sT,
                        int64_t q_sH, int64_t k_sT, int64_t k_sH, int64_t v_sT, int64_t v_sH,
-                       float scale, void* out, void* stream) {
+                       float scale, void* out, int32_t* status, void* stream) {
   if (!rows || n_rows <= 0 || N <= 0) return SOLATTN_ERR_ARG;
   // One batch: the n_rows gathered query rows against all N keys (all-exact route, so the
   // K/V pointers stand in for the pooled statistics), written to out[rows].
   return attention_impl(q, k, v, 1, n_rows, N, H, D, 0, q_sT, q_sH, 0, k_sT, k_sH, 0, v_sT, v_sH,
                         rows, nullptr, N, k, v, nullptr, nullptr, nullptr, scale,
-                        SOLATTN_FORCE_ALL, -1, 0, 0, out, rows, N, nullptr, nullptr, nullptr,
+                        SOLATTN_FORCE_ALL, -1, 0, 0, out, rows, N, nullptr, nullptr, status,
                         nullptr, stream);
 }
 
 int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,
                   int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH, int64_t k_sB,
                   int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT, int64_t v_sH,
-                  float scale, void* out, void* stream) {
+                  float scale, void* out, int32_t* status, void* stream) {
   // All-exact route: no pooled statistics are read (kc/vc are only dereferenced for
   // centroid tiles, and force = 1 produces none), so the K/V pointers stand in for them.
   return solattn_attention(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
                            v_sT, v_sH, nullptr, nullptr, 0, k, v, nullptr, nullptr, nullptr, scale,
-                           SOLATTN_FORCE_ALL, -1, 0, 0, out, nullptr, nullptr, nullptr, stream);
+                           SOLATTN_FORCE_ALL, -1, 0, 0, out, nullptr, status, nullptr, stream);
 }
 
 int solattn_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
@@ -419,6 +426,14 @@ int solattn_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_p
       direction == 0 ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost,
       static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SOLATTN_OK : SOLATTN_ERR_CUDA;
+}
+
+int solattn_status_to_host(const int32_t* status, int32_t* host_dst, void* stream) {
+  if (!status || !host_dst) return SOLATTN_ERR_ARG;
+  return cudaMemcpyAsync(host_dst, status, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                         static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? SOLATTN_OK
+             : SOLATTN_ERR_CUDA;
 }
 
 int solattn_read_status(int32_t* status, int32_t* value, void* stream) {

@@ -37,9 +37,13 @@ SIGNATURES = {
                                + [_P, _P, _I64, _P]
                                + [c_float, c_float, c_int, c_int, c_int, _P, _I64, _P, _P, _I64,
                                   _P, _P]),
-    "solattn_dense": (c_int, [_P, _P, _P] + [_I64] * 5 + [_I64] * 9 + [c_float, _P, _P]),
-    "solattn_dense_rows": (c_int, [_P, _P, _P, _P] + [_I64] * 4 + [_I64] * 6 + [c_float, _P, _P]),
+    "solattn_dense": (c_int, [_P, _P, _P] + [_I64] * 5 + [_I64] * 9 + [c_float, _P, _P, _P]),
+    "solattn_dense_rows": (c_int, [_P, _P, _P, _P] + [_I64] * 4 + [_I64] * 6
+                           + [c_float, _P, _P, _P]),
     "solattn_read_status": (c_int, [_P, _P, _P]),
+    "solattn_status_to_host": (c_int, [_P, _P, _P]),
+    "solattn_noalloc_scratch_address": (c_int, [POINTER(c_void_p)]),
+    "solattn_noalloc_read_status": (c_int, [_P, _P]),
     "solattn_sol_forward_noalloc": (c_int, [_P, _P, _P] + [_I64] * 5 + [_I64] * 9
                                     + [_P, _P, _I64, _P]
                                     + [c_float, c_float, c_int, c_int, c_int, _P, _P, _P]),

@@ -9,15 +9,14 @@ current stream; there is no fallback path.
 from __future__ import annotations
 
 import math
-import os
 from dataclasses import dataclass
 
 import torch
 
 from . import _lib
+from .status import check_device_errors, monitor
 
 BLOCK = 64
-_CHECK_STATUS = os.environ.get("SOLATTN_CHECK_STATUS", "0") == "1"
 _DEVICE_OK = {}
 
 
@@ -32,6 +31,9 @@ class SolStats:
     key_blocks: int
 
     def density(self) -> float:
+        # Synchronises anyway: first raise if a call on this device reported a device error.
+        if self.exact_blocks.is_cuda:
+            check_device_errors(self.exact_blocks.device)
         if isinstance(self.key_blocks, torch.Tensor):
             return (self.exact_blocks.float() / self.key_blocks).mean().item()
         return self.exact_blocks.float().mean().item() / self.key_blocks
@@ -45,7 +47,7 @@ def _is_b200(device: torch.device) -> bool:
 
 
 def _validate(q, k, v, scale):
-    """Input contract of ``attention.py:25-45`` (device check re-targeted to sm_100a)."""
+    """Input contract of ``attention.py:19-44`` (device check re-targeted to sm_100a)."""
     if any(t.ndim != 4 for t in (q, k, v)):
         raise ValueError("Q/K/V must have BTHD rank-4 layout")
     if (k.shape != v.shape or q.shape[0] != k.shape[0]
@@ -109,6 +111,8 @@ def launch_sol(q, k, v, scale, beta, local, kv_sink, q_sink, stats, protection=N
         out_shape = tuple(q.shape)
     nqb = (Tq + BLOCK - 1) // BLOCK
     L = _lib.load()
+    mon = monitor(q.device)
+    mon.poll(wait=False)  # an earlier call's device-side error surfaces here
     total, offs = _lib.workspace_layout(B, Tq, Tk, H, D)
     if total <= 0:
         raise _lib.SolAttnError("unsupported shape for libsolattn")
@@ -118,7 +122,8 @@ def launch_sol(q, k, v, scale, beta, local, kv_sink, q_sink, stats, protection=N
     if not scatter:
         out = torch.empty(out_shape, dtype=torch.bfloat16, device=q.device)
     counts = torch.empty((B, nqb, H), dtype=torch.int32, device=q.device)
-    stream = torch.cuda.current_stream(q.device).cuda_stream
+    tstream = torch.cuda.current_stream(q.device)
+    stream = tstream.cuda_stream
     args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), B, Tq, Tk, H, D,
             *_strides(q, indexed), *_strides(k, indexed), *_strides(v, indexed),
             rows.data_ptr() if indexed else None, keys.data_ptr() if indexed else None,
@@ -138,22 +143,21 @@ def launch_sol(q, k, v, scale, beta, local, kv_sink, q_sink, stats, protection=N
     else:
         rc = L.solattn_sol_forward(*args, counts.data_ptr() if stats else None, stream)
         _lib.check(rc, "solattn_sol_forward")
-    if _CHECK_STATUS:
-        check_status(ws_ptr + offs["status"], stream)
+    # The call's status word (cleared by the call itself) travels to pinned host memory
+    # asynchronously; the next call or SolStats.density() looks at it.
+    mon.record(ws_ptr + offs["status"], tstream)
     return out, counts
 
 
-def check_status(status_ptr: int, stream: int) -> None:
-    """Synchronise and raise if a kernel reported a device-side error (diagnostics only)."""
-    import ctypes
-    value = ctypes.c_int32(0)
-    rc = _lib.load().solattn_read_status(status_ptr, ctypes.byref(value), stream)
-    if rc != 0:
-        raise _lib.SolAttnError(f"device-side status {value.value} ({_lib.load().solattn_strerror(rc).decode()})")
+def _dense_status(device):
+    """A zeroed device status word for the dense entry points, after polling earlier calls."""
+    mon = monitor(device)
+    mon.poll(wait=False)
+    return mon, torch.zeros(4, dtype=torch.int32, device=device)
 
 
 def dense_attention(q, k, v, *, scale=None):
-    """Noncausal BF16 attention over all keys, FP32 softmax/accumulation (``attention.py:53-61``).
+    """Noncausal BF16 attention over all keys, FP32 softmax/accumulation (``attention.py:47-55``).
 
     Runs the all-exact route of the fused sm_100a kernel.
     """
@@ -161,12 +165,15 @@ def dense_attention(q, k, v, *, scale=None):
     with torch.no_grad(), torch.cuda.device(q.device):
         q, k, v = (x if _aligned(x) else x.contiguous() for x in (q, k, v))
         B, Tq, H, D = q.shape
+        mon, status = _dense_status(q.device)
         out = torch.empty(tuple(q.shape), dtype=torch.bfloat16, device=q.device)
-        stream = torch.cuda.current_stream(q.device).cuda_stream
+        tstream = torch.cuda.current_stream(q.device)
         rc = _lib.load().solattn_dense(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, Tq,
                                        k.shape[1], H, D, *_strides(q, False), *_strides(k, False),
-                                       *_strides(v, False), float(scale), out.data_ptr(), stream)
+                                       *_strides(v, False), float(scale), out.data_ptr(),
+                                       status.data_ptr(), tstream.cuda_stream)
         _lib.check(rc, "solattn_dense")
+        mon.record(status.data_ptr(), tstream)
         return out
 
 
@@ -195,12 +202,14 @@ def dense_attention_rows(q, k, v, rows, *, scale=None, out=None):
         if out is None:
             out = torch.empty_like(q, memory_format=torch.contiguous_format)
         N, H, D = q.shape
-        stream = torch.cuda.current_stream(q.device).cuda_stream
+        mon, status = _dense_status(q.device)
+        tstream = torch.cuda.current_stream(q.device)
         rc = _lib.load().solattn_dense_rows(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), rows.data_ptr(), rows.numel(), N, H, D,
             q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
-            float(scale), out.data_ptr(), stream)
+            float(scale), out.data_ptr(), status.data_ptr(), tstream.cuda_stream)
         _lib.check(rc, "solattn_dense_rows")
+        mon.record(status.data_ptr(), tstream)
         return out
 
 
@@ -217,7 +226,7 @@ def _check_out(out, q):
 
 def sol_attention(q, k, v, *, beta=1.0, scale=None, local_blocks=1,
                   kv_sink_tokens=0, query_sink_tokens=0, return_stats=False):
-    """SOL-style noncausal attention; no semantic mask support (``attention.py:64-91``).
+    """SOL-style noncausal attention; no semantic mask support (``attention.py:58-85``).
 
     Physical blocks contain 64 tokens. Selected blocks use BF16 QK/PV with FP32
     softmax/accumulation; other blocks contribute pooled-key/value correction.

@@ -1,6 +1,6 @@
 """Host-resident inputs: SOL attention on BTHD tensors that live in (pinned) host memory.
 
-The reference's API (``attention.py:64-91``) takes device tensors only; a caller whose Q/K/V sit
+The reference's API (``attention.py:58-85``) takes device tensors only; a caller whose Q/K/V sit
 in host memory must copy them to the GPU first, then copy the output back.  Heads are
 independent, so ``sol_attention_host`` streams them through the GPU in groups instead: while
 group g is pooled, routed and attended to, the inputs of group g + 1 are on their way in and the

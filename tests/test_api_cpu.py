@@ -1,4 +1,4 @@
-"""Host-side API contract (``src/sol_attn_amd/attention.py:25-91``) without a GPU."""
+"""Host-side API contract (``src/sol_attn_amd/attention.py:19-85``) without a GPU."""
 
 import math
 
@@ -70,15 +70,16 @@ def test_scatter_and_dense_rows_reject_bad_arguments_on_cpu():
 
 
 def test_bench_receipt_rejects_bad_runs_before_touching_the_gpu(tmp_path):
-    """The receipt keeps the reference's guards (``bench_attention.py:61-66``): finite beta,
-    positive counts, and a fresh output path (receipts are never overwritten)."""
+    """Receipts are comparable only for finite beta and positive counts, and a receipt that
+    exists is never replaced (the reference keeps the same guards,
+    ``benchmarks/bench_attention.py:61-66``); all of it is checked before any GPU work."""
     from sol_attn_b200 import bench_receipt
     out = tmp_path / "r.json"
     with pytest.raises(SystemExit):
-        bench_receipt.main(["--beta", "inf", "--out", str(out)])
+        bench_receipt.main([str(out), "--beta", "inf"])
     with pytest.raises(SystemExit):
-        bench_receipt.main(["--tokens", "0", "--out", str(out)])
+        bench_receipt.main([str(out), "--tokens", "0"])
     out.write_text("{}")
     with pytest.raises(SystemExit):
-        bench_receipt.main(["--out", str(out)])
+        bench_receipt.main([str(out)])
     assert out.read_text() == "{}"

@@ -89,8 +89,17 @@ def test_scatter_and_dense_rows_reject_bad_arguments():
     assert L.solattn_sol_forward_scatter(*common, None, None, 0, *tail, 64, None, None) == -1
     assert L.solattn_sol_forward_scatter(*common, 16, None, 64, *tail, 0, None, None) == -1
     assert L.solattn_dense_rows(16, 16, 16, None, 4, 64, 1, 64, 64, 64, 64, 64, 64, 64, 0.125,
-                                16, None) == -1
+                                16, None, None) == -1
     assert L.solattn_dense_rows(16, 16, 16, 16, 0, 64, 1, 64, 64, 64, 64, 64, 64, 64, 0.125,
-                                16, None) == -1
+                                16, None, None) == -1
     assert L.solattn_dense_rows(16, 16, 16, 16, 4, 64, 1, 96, 64, 64, 64, 64, 64, 64, 0.125,
-                                16, None) == -2
+                                16, None, None) == -2
+
+
+def test_status_entry_points_reject_null_pointers():
+    """The status copy and the no-allocation status accessors check their pointers first."""
+    L = _lib.load()
+    assert L.solattn_status_to_host(None, 16, None) == -1
+    assert L.solattn_status_to_host(16, None, None) == -1
+    assert L.solattn_noalloc_read_status(None, None) == -1
+    assert L.solattn_noalloc_scratch_address(None) == -1
