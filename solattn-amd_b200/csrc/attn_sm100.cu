@@ -33,11 +33,12 @@
 //              written over the S buffer, arrive P_FULL.  A warp whose q-block does not use
 //              the tile writes P = 0 without reading S.  Item epilogue: merge O_0 and O_1 ->
 //              BF16, then O_FREE (the next item's P V may overwrite O).
-//   warps 8-9  S issue for even / odd tiles (lane 0 issues; the whole warp runs the loop so
-//              that addresses stay warp-uniform): S_g = Q K_g^T once P_{g-kStages} V has freed
-//              the buffer and K_g has landed.  One thread issues a dependent tcgen05.mma about
-//              every 100 cycles; two issuers keep the 8 MMAs (N = 64) per tile flowing.
-//   warp 10    P V issue: O_{g%2} += P_g V_g once the group's four warps have written P_g.
+//   warps 8-9  S issue for even / odd tiles (the whole warp runs the loop so that operands stay
+//              warp-uniform; one elected lane issues): S_g = Q K_g^T once P_{g-kStages} V has
+//              freed the buffer and K_g has landed; two issuers keep the 8 MMAs (N = 64) per tile
+//              flowing.
+//   warp 10    P V issue (likewise warp-uniform): O_{g%2} += P_g V_g once the group's four warps
+//              have written P_g.
 //   warp 11    producer: per item, the routing bitmasks, the tile list and the exact-block
 //              counts (built one item ahead), Q; then the K ring (slot refilled when S has
 //              completed) and the V ring (slot refilled when P V has completed), by TMA, or by
@@ -775,17 +776,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         if (p.k.idx) fence_proxy_async_smem();  // gathered V rows were written by cp.async
-        if (lane == 0) {
-          if (i < real) {
-            const uint64_t vd = dV + (uint64_t)s * kSlotStep;
-            const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
-            const uint32_t tO = tmem + kTmemO + (uint32_t)(128 * (gi & 1));  // the tile's group
-            // Local tiles 0 and 1 are each group's first of the item (items start at even
-            // tile positions): they start the accumulator.
+        // Operands are computed by the whole warp (warp-uniform) and one elected lane issues: a
+        // tcgen05.mma issued from a branch that only lane 0 runs took up to twice as long.
+        const uint64_t vd = dV + (uint64_t)s * kSlotStep;
+        const uint32_t tP = tmem + kTmemS + (uint32_t)(kKeys * s);
+        const uint32_t tO = tmem + kTmemO + (uint32_t)(128 * (gi & 1));  // the tile's group
+        // Local tiles 0 and 1 are each group's first of the item (items start at even tile
+        // positions): they start the accumulator.
+        const uint32_t acc0 = i > 1 ? 1u : 0u;
+        const bool has_keys = i < real;
+        if (elect_one()) {
+          if (has_keys) {
 #pragma unroll
             for (int kk = 0; kk < kKeys / 16; ++kk)
               mma_ts(tO, tP + (uint32_t)(8 * kk), vd + (uint64_t)((kk * 16 * 128) >> 4), idO,
-                     (i > 1 || kk > 0) ? 1u : 0u);
+                     kk > 0 ? 1u : acc0);
           }
           mma_commit(bar(PV_DONE + s));  // a padding tile: once the MMAs before it completed
         }
@@ -836,10 +841,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         if (p.k.idx) fence_proxy_async_smem();  // gathered K rows were written by cp.async
-        if (lane == 0) {
-          if (i < real) {
-            const uint64_t kd = dK + (uint64_t)s * kSlotStep;
-            const uint32_t tS = tmem + kTmemS + (uint32_t)(kKeys * s);
+        const uint64_t kd = dK + (uint64_t)s * kSlotStep;
+        const uint32_t tS = tmem + kTmemS + (uint32_t)(kKeys * s);
+        const bool has_keys = i < real;
+        if (elect_one()) {
+          if (has_keys) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint64_t off = (uint64_t)(((kk >> 2) * kQBox + (kk & 3) * 32) >> 4);
