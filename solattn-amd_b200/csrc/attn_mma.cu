@@ -1,5 +1,6 @@
 // Fused routed attention, 64-row q-block per CTA, mma.sync BF16 tiles.
-// (Replaces `_sol`, kernels.py:101-182.)
+// (Replaces `_sol`, kernels.py:101-182.)  Runs only for more than 4096 key blocks
+// (T > 262144 keys); every other launch takes the tcgen05 kernel of attn_sm100.cu.
 //
 // CTA = 4 warps, one (b, h, q-block); warp w owns rows 16w..16w+15.
 //   1. Prologue: Q tile -> shared (cp.async, zero-filled past Tq); routing of every key block
@@ -351,8 +352,9 @@ namespace solattn {
 cudaError_t launch_attn_sm100(const AttnParams& p, int D, cudaStream_t stream);
 bool attn_sm100_supported(const AttnParams& p);
 
-// BTHD inputs run on the tcgen05/TMA kernel; gathered (indexed) rows and more than 4096 key
-// blocks use this kernel until the tcgen05 kernel gains a gather producer and a chunked tile list.
+// Every call runs on the tcgen05/TMA kernel except one with more than 4096 key blocks
+// (T > 262144 keys), which the int16 tile list of that kernel cannot address: only that size
+// reaches this mma.sync kernel.
 cudaError_t launch_attention(const AttnParams& p, int D, cudaStream_t stream) {
   if (attn_sm100_supported(p))
     return launch_attn_sm100(p, D, stream);

@@ -1173,11 +1173,10 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
 
 }  // namespace
 
-// The softmax folds a positive scale into the exponent (max(s) * scale == max(s * scale) and
-// masked -inf scores stay -inf), so other scales take the mma.sync kernel.
-bool attn_sm100_supported(const AttnParams& p) {
-  return p.nkb <= kMaxKeyBlocks && p.scale_log2 > 0.f && (p.masks != nullptr || p.force != 0);
-}
+// The int16 tile list holds at most kMaxKeyBlocks key blocks.  Every entry point has already
+// rejected scales <= 0 (the softmax folds the positive scale into its exponent FMA) and a
+// threshold route without routing masks, so the key-block count is the only limit left.
+bool attn_sm100_supported(const AttnParams& p) { return p.nkb <= kMaxKeyBlocks; }
 
 cudaError_t launch_attn_sm100(const AttnParams& p, int D, cudaStream_t stream) {
   return D == 128 ? launch_sm100<128>(p, stream) : launch_sm100<64>(p, stream);
