@@ -11,10 +11,11 @@ bit identity:
 * pooling (``solattn_pool_qkv``): 8 row groups, group g sums rows g, g+8, ..., g+56 of the
   block in order (rows past the ragged end skipped), the group sums are added in order
   g = 0..7, mean = sum / count; K/V means rounded to BF16 (nearest even);
-* moments (``solattn_threshold``): sequential sums over key blocks of x and x*x,
+* moments (``solattn_threshold``): eight slice sums per channel, slice j summing key blocks
+  j, j+8, j+16, ... of x and x*x in order, combined as ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7));
   mean = s1/n, var = max(s2/n - mean*mean, 0);
-* cutoff: sequential sums over d of qc*mean and (qc*qc)*var,
-  cutoff = (mu + beta*sqrt(sg)) * scale;
+* cutoff: eight partial sums over d = 8i + e (i increasing) of qc*mean and (qc*qc)*var,
+  combined in the same tree; cutoff = (mu + beta*sqrt(sg)) * scale;
 * routing (fused kernel prologue): proxy = dot * scale where dot sums qc*kc as eight
   partial sums p_j over d = 8i + j (i increasing) combined as
   ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); exact iff proxy > cutoff (force modes and the local / sink / protected rules as in
@@ -57,29 +58,45 @@ def pool(x: torch.Tensor, out_bf16: bool) -> np.ndarray:
     return _bf16_round(mean) if out_bf16 else mean.astype(F32)
 
 
+def _tree8(p):
+    """((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)) of eight float32 arrays."""
+    return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]))
+
+
 def moments(kc: np.ndarray):
     """kc [B, H, nkb, D] (BF16 values as float32) -> mean, var [B, H, D]."""
-    n = F32(kc.shape[2])
-    s1 = np.zeros(kc.shape[:2] + kc.shape[3:], F32)
-    s2 = np.zeros_like(s1)
-    for j in range(kc.shape[2]):
-        x = kc[:, :, j]
-        s1 = s1 + x
-        s2 = s2 + x * x
-    mean = s1 / n
-    var = np.maximum(s2 / n - mean * mean, F32(0))
+    nb = kc.shape[2]
+    n = F32(nb)
+    s1, s2 = [], []
+    for j in range(8):
+        a = np.zeros(kc.shape[:2] + kc.shape[3:], F32)
+        b = np.zeros_like(a)
+        for r in range(j, nb, 8):
+            x = kc[:, :, r]
+            a = a + x
+            b = b + x * x
+        s1.append(a)
+        s2.append(b)
+    mean = _tree8(s1) / n
+    var = np.maximum(_tree8(s2) / n - mean * mean, F32(0))
     return mean, var
 
 
 def cutoffs(qc: np.ndarray, mean: np.ndarray, var: np.ndarray, beta: float, scale: float):
     """qc [B, H, nqb, D] -> cutoff [B, H, nqb]."""
-    mu = np.zeros(qc.shape[:3], F32)
-    sg = np.zeros_like(mu)
-    for e in range(qc.shape[3]):
-        qv = qc[..., e]
-        mu = mu + qv * mean[:, :, None, e]
-        sg = sg + (qv * qv) * var[:, :, None, e]
-    return (mu + F32(beta) * np.sqrt(sg)) * F32(scale)
+    D = qc.shape[3]
+    mu, sg = [], []
+    for e in range(8):
+        a = np.zeros(qc.shape[:3], F32)
+        b = np.zeros_like(a)
+        for i in range(D // 8):
+            d = 8 * i + e
+            qv = qc[..., d]
+            a = a + qv * mean[:, :, None, d]
+            b = b + (qv * qv) * var[:, :, None, d]
+        mu.append(a)
+        sg.append(b)
+    return (_tree8(mu) + F32(beta) * np.sqrt(_tree8(sg))) * F32(scale)
 
 
 def route(qc, kc, cutoff, scale, force, local, kv_sink_blocks, q_sink_blocks, protect=None):

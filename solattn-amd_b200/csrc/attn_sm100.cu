@@ -7,7 +7,8 @@
 // 128-row query tile = two 64-row q-blocks (qb0, qb0 + 1) of one (b, h).  Launch order: first
 // the q-block pairs holding query-sink blocks of all heads (every key block exact: the longest
 // items), then each head's remaining pairs head by head (the items in flight at one time share
-// one head's K/V in L2).  384 threads.
+// one head's K/V in L2), within a head most tiles first (the routing pass sorts them), so that
+// the launch ends on its shortest items.  384 threads.
 //
 // Tiles hold 64 keys: one exact key block, or 64 pooled centroids.  The routing pass
 // (route.cu) has already written every q-block's exact-block bitmask; an item's tile list
@@ -226,33 +227,40 @@ __device__ __forceinline__ float row_max64(const uint32_t (&s)[2][32]) {
 }
 
 
-// Position of work item `item` in the launch order: the q-block pairs holding query-sink blocks
-// of every head first (the longest items: every key block exact), then each head's remaining
-// pairs, head by head.
+// A work item is a q-block pair, identified by its pair id bh * npairs + pair.
 struct ItemPos {
   int b, h, bh, qb0;
 };
-__device__ __forceinline__ ItemPos item_pos(int item, int nqb, int q_sink_blocks, int B, int H) {
+__device__ __forceinline__ ItemPos item_at(int pid, int nqb, int H) {
   const int npairs = (nqb + 1) / 2;
-  const int sink_pairs = min(npairs, (q_sink_blocks + 1) / 2);
-  int bh, pair;
-  if (item < sink_pairs * B * H) {
-    bh = item / sink_pairs;
-    pair = item % sink_pairs;
-  } else {
-    const int r = item - sink_pairs * B * H, rest = npairs - sink_pairs;
-    bh = r / rest;
-    pair = sink_pairs + r % rest;
-  }
   ItemPos ip;
-  ip.bh = bh;
-  ip.b = bh / H;
-  ip.h = bh % H;
-  ip.qb0 = 2 * pair;
+  ip.bh = pid / npairs;
+  ip.b = ip.bh / H;
+  ip.h = ip.bh % H;
+  ip.qb0 = 2 * (pid % npairs);
   return ip;
 }
-__device__ __forceinline__ ItemPos item_pos(const AttnParams& p, int item) {
-  return item_pos(item, p.nqb, p.q_sink_blocks, p.B, p.H);
+
+// The pair id of the launch's claim number `claim`: first the pairs holding query-sink blocks
+// of every head (the longest items: every key block exact, so none of them may start last),
+// then each head's remaining pairs, head by head (the items in flight at one time share one
+// head's K/V in L2), within a head in the routing pass's order, most tiles first, where it
+// wrote one for this call (stamp == epoch), else in q-block order.
+__device__ __forceinline__ int claim_pair(const AttnParams& p, int claim) {
+  const int npairs = (p.nqb + 1) / 2;
+  const int sink = min(npairs, (p.q_sink_blocks + 1) / 2);
+  const int sink_items = sink * p.B * p.H;
+  if (claim < sink_items) return (claim / sink) * npairs + claim % sink;
+  const int r = claim - sink_items, rest = npairs - sink;
+  if (rest <= 0) return 0;  // (claims stop below sink_items then)
+  const int bh = r / rest, j = r % rest;
+  int pair = sink + j;
+  if (p.order) {
+    const uint32_t st = __ldg(p.stamp + bh);
+    const int o = __ldg(p.order + (int64_t)bh * npairs + j);
+    if (st == p.epoch && o >= sink && o < npairs) pair = o;
+  }
+  return bh * npairs + pair;
 }
 
 // An item's routing mask words (both q-blocks, 2 nwords <= 256 words), loaded into registers one
@@ -261,15 +269,17 @@ constexpr int kMaskRegs = 2 * (kMaxKeyBlocks / 32) / 32;
 struct MaskWords {
   uint32_t w[kMaskRegs];
   int ntiles, real;  // from the item's precomputed list header (when the routing pass built it)
+  int pid;           // the claimed item's pair id
 };
-__device__ __forceinline__ MaskWords load_mask_words(const AttnParams& p, int item, int total,
+__device__ __forceinline__ MaskWords load_mask_words(const AttnParams& p, int claim, int total,
                                                      int nwords, int lane) {
   MaskWords mw;
 #pragma unroll
   for (int j = 0; j < kMaskRegs; ++j) mw.w[j] = 0u;
   mw.ntiles = mw.real = 0;
-  if (!p.masks || item >= total) return mw;
-  const ItemPos ip = item_pos(p, item);
+  mw.pid = claim < total ? claim_pair(p, claim) : 0;
+  if (!p.masks || claim >= total) return mw;
+  const ItemPos ip = item_at(mw.pid, p.nqb, p.H);
   if (p.lists) {
     const int2 hdr = __ldg(reinterpret_cast<const int2*>(
         p.lists + ((int64_t)ip.bh * ((p.nqb + 1) / 2) + (ip.qb0 >> 1)) * item_list_stride(p.nkb)));
@@ -332,10 +342,10 @@ __device__ __forceinline__ int build_tile_list(const AttnParams& p, const ItemPo
 template <int D>
 __device__ __forceinline__ bool item_epilogue(uint32_t tmem, uint32_t bar0, int warp, int lane, int k,
                                            int last, float m_run, float l_run, int ntiles, int g,
-                                           int item, float* sMerge, volatile int* abort_flag,
+                                           int pid, float* sMerge, volatile int* abort_flag,
                                            int32_t* status, __nv_bfloat16* out,
                                            const int64_t* out_idx, int64_t out_rows, int Tq, int H,
-                                           int nqb, int q_sink_blocks, int B) {
+                                           int nqb) {
   auto bar = [bar0](int i) { return bar0 + 8u * (uint32_t)i; };
   const int quarter = warp & 3, grp = warp >> 2, lb = k & 1;
   const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
@@ -361,7 +371,7 @@ __device__ __forceinline__ bool item_epilogue(uint32_t tmem, uint32_t bar0, int 
   // A group without tiles in this item holds another item's accumulator: it is skipped.
   const bool has0 = ntiles >= 2 || (ntiles == 1 && (g & 1) == 0);
   const bool has1 = ntiles >= 2 || (ntiles == 1 && (g & 1) == 1);
-  const ItemPos ip = item_pos(item, nqb, q_sink_blocks, B, H);
+  const ItemPos ip = item_at(pid, nqb, H);
   const int grow = ip.qb0 * kBlock + quarter * 32 + lane;
   // This warp writes head dims [grp * D / 2, (grp + 1) * D / 2) of its 32 rows: row grow of
   // batch b, or (scatter) output row out_idx[b * Tq + grow].
@@ -525,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         break;
       }
-      const ItemPos ip = item_pos(p, item);
+      const int pid = mw.pid;  // the claimed item (mw holds its words until the next load)
+      const ItemPos ip = item_at(pid, p.nqb, p.H);
       // Q of the item first: it does not depend on the tile list.
       if (k >= 2 && !warp_wait(bar(Q_EMPTY + lb), (uint32_t)((k >> 1) - 1) & 1u, abort_flag,
                                p.status)) {
@@ -562,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           build_tile_list(p, ip, mw, sMask + lb * 2 * nwords, tl, nwords, tk, lane, real);
       if (lane == 0) {
         misc[2 + lb] = (uint32_t)ntiles;
-        misc[4 + lb] = (uint32_t)item;
+        misc[4 + lb] = (uint32_t)pid;
         misc[6 + lb] = (uint32_t)real;
         misc[8 + lb] = (uint32_t)tk;
         if (p.lists) {
@@ -886,7 +897,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int item = (int)vmisc[4 + lb];
       if (item < 0) break;
       const int ntiles = (int)vmisc[2 + lb];
-      const ItemPos ip = item_pos(p, item);
+      const ItemPos ip = item_at(item, p.nqb, p.H);
       // The warp's q-block exists (only the last pair of a head can lack its second q-block).
       const bool warp_rows = qsel == 0 || ip.qb0 + 1 < p.nqb;
       // The batch's keys (its own count in a ragged launch) and its last, maybe partial, block.
@@ -1069,7 +1080,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Tiles with keys decide which accumulators hold this item.
       if (!item_epilogue<D>(tmem, bar0, warp, lane, k, last, m_run, l_run, (int)vmisc[6 + lb], g,
                             (int)vmisc[4 + lb], sMerge, abort_flag, p.status, p.out, p.out_idx,
-                            p.out_rows, p.Tq, p.H, p.nqb, p.q_sink_blocks, p.B))
+                            p.out_rows, p.Tq, p.H, p.nqb))
         break;
       g += ntiles;
     }

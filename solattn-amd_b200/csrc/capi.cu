@@ -4,6 +4,8 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "../../include/solattn.h"
 #include "common.cuh"
 
@@ -67,11 +69,13 @@ struct Layout {
 };
 
 // Bytes of the routing-mask buffer: the bitmask words, the work counter (padded to 16 bytes),
-// then one tile list per q-block pair (common.cuh: item_list_stride).
+// one tile list per q-block pair (common.cuh: item_list_stride), then the item-order section
+// (common.cuh: order_section_bytes).
 int64_t masks_bytes(int64_t B, int64_t Tq, int64_t Tk, int64_t H) {
   const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
   const int64_t words = (B * H * nqb * cdiv(nkb, 32) + 1 + 3) & ~int64_t(3);
-  return 4 * words + B * H * cdiv(nqb, 2) * item_list_stride((int)nkb);
+  return 4 * words + B * H * cdiv(nqb, 2) * item_list_stride((int)nkb) +
+         order_section_bytes(B * H, cdiv(nqb, 2));
 }
 
 // The tile lists inside a mask buffer.
@@ -82,12 +86,37 @@ uint8_t* lists_of(uint32_t* masks, int64_t B, int64_t Tq, int64_t Tk, int64_t H)
   return reinterpret_cast<uint8_t*>(masks) + 4 * words;
 }
 
+// The item-order section inside a mask buffer (after the tile lists) into p.arrive, p.stamp and
+// p.order, with a fresh nonzero epoch.  Epochs come from one process-wide counter, so a stamp
+// left by an earlier call never matches.
+std::atomic<uint32_t> g_epoch{0};
+void set_item_order(AttnParams& p, uint32_t* masks, int64_t B, int64_t Tq, int64_t Tk,
+                    int64_t H) {
+  p.arrive = nullptr;
+  p.stamp = nullptr;
+  p.order = nullptr;
+  p.epoch = 0;
+  if (!masks) return;
+  const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock), bh = B * H;
+  uint8_t* sec = lists_of(masks, B, Tq, Tk, H) + bh * cdiv(nqb, 2) * item_list_stride((int)nkb);
+  p.arrive = reinterpret_cast<int32_t*>(sec);
+  p.stamp = reinterpret_cast<uint32_t*>(sec) + order_words_padded(bh);
+  p.order = reinterpret_cast<int32_t*>(sec) + 2 * order_words_padded(bh);
+  uint32_t e;
+  do {
+    e = g_epoch.fetch_add(1u, std::memory_order_relaxed) + 1u;
+  } while (e == 0u);
+  p.epoch = e;
+}
+
 Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   Layout L;
   const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
   int64_t off = 0;
+  // The status word, then (at byte 16) the routing pass's per-head arrival counters, which
+  // solattn_sol_forward zeroes together with the status word before every call.
   L.status = off;
-  off = align256(off + 16);
+  off = align256(off + 16 + 4 * B * H);
   L.kc = off;
   off = align256(off + B * H * nkb * D * 2);
   L.vc = off;
@@ -224,7 +253,7 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
                    const uint8_t* protect, float scale, int force, int local,
                    int kv_sink_blocks, int q_sink_blocks, void* out, const int64_t* out_idx,
                    int64_t out_rows, const int32_t* key_counts, int32_t* counts, int32_t* status,
-                   uint32_t* masks, void* stream) {
+                   uint32_t* masks, int32_t* arrive, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (!q || !k || !v || !kc || !vc || !out) return SOLATTN_ERR_ARG;
@@ -258,6 +287,8 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
   p.status = status;
   p.masks = masks;
   p.lists = lists_of(masks, B, Tq, Tk, H);
+  set_item_order(p, masks, B, Tq, Tk, H);
+  if (arrive && p.arrive) p.arrive = arrive;  // counters the caller zeroed for this call
   p.B = (int)B;
   p.Tq = (int)Tq;
   p.Tk = (int)Tk;
@@ -307,7 +338,8 @@ int sol_forward_impl(const void* q, const void* k, const void* v, int64_t B, int
   void* vc = ws + L.vc;
   float* cutoff = reinterpret_cast<float*>(ws + L.cutoff);
   int32_t* status = reinterpret_cast<int32_t*>(ws + L.status);
-  if (cudaMemsetAsync(status, 0, sizeof(int32_t), static_cast<cudaStream_t>(stream)) !=
+  // The status word and the routing pass's arrival counters (byte 16 on) in one memset.
+  if (cudaMemsetAsync(status, 0, (size_t)(16 + 4 * B * H), static_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
     return SOLATTN_ERR_CUDA;
   rc = pool_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT, v_sH,
@@ -327,7 +359,8 @@ int sol_forward_impl(const void* q, const void* k, const void* v, int64_t B, int
                         force == SOLATTN_FORCE_THRESHOLD ? qc : nullptr,
                         force == SOLATTN_FORCE_THRESHOLD ? cutoff : nullptr, protect, scale, force,
                         local, kv_sink_blocks, q_sink_blocks, out, out_idx, out_rows, key_counts,
-                        counts, status, reinterpret_cast<uint32_t*>(ws + L.masks), stream);
+                        counts, status, reinterpret_cast<uint32_t*>(ws + L.masks), status + 4,
+                        stream);
 }
 
 }  // namespace
@@ -345,7 +378,7 @@ int solattn_attention(const void* q, const void* k, const void* v, int64_t B, in
   return attention_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT,
                         v_sH, q_idx, kv_idx, idx_rows, kc, vc, qc, cutoff, protect, scale, force,
                         local, kv_sink_blocks, q_sink_blocks, out, nullptr, 0, nullptr, counts,
-                        status, masks, stream);
+                        status, masks, nullptr, stream);
 }
 
 int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
@@ -402,7 +435,7 @@ int solattn_dense_rows(const void* q, const void* k, const void* v, const int64_
   return attention_impl(q, k, v, 1, n_rows, N, H, D, 0, q_sT, q_sH, 0, k_sT, k_sH, 0, v_sT, v_sH,
                         rows, nullptr, N, k, v, nullptr, nullptr, nullptr, scale,
                         SOLATTN_FORCE_ALL, -1, 0, 0, out, rows, N, nullptr, nullptr, status,
-                        nullptr, stream);
+                        nullptr, nullptr, stream);
 }
 
 int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,

@@ -41,6 +41,16 @@ struct AttnParams {
                             // (read by attn_sm100_kernel) or by attn_mma_kernel
   uint8_t* lists;           // per-item tile lists (see item_list_stride) written by route.cu, or
                             // nullptr (the fused kernel then builds them itself)
+  // Item order (with lists only; else nullptr): route.cu sorts each head's q-block pairs after
+  // the sink pairs by tile count, longest first, and the fused kernel hands them out in that
+  // order.  arrive[B * H] counts the routing CTAs of a head that have written their lists (zero
+  // when the routing pass starts, and the pass leaves it zero); the last one writes the head's
+  // order[B * H, npairs] and stamp[B * H] = epoch.  The order is used only where the stamp
+  // equals this call's epoch, so a head without a sorted order keeps the natural one.
+  int32_t* arrive;
+  uint32_t* stamp;
+  int32_t* order;
+  uint32_t epoch;
   int B, Tq, Tk, H, nqb, nkb;
   const int32_t* tk_b;  // optional per-batch key counts [B] (ragged indexed plans: batch b has
                         // tk_b[b] <= Tk keys, ceil(tk_b[b] / 64) key blocks), else nullptr
@@ -200,6 +210,13 @@ __host__ __device__ inline int item_list_capacity(int nkb) {
 }
 __host__ __device__ inline int64_t item_list_stride(int nkb) {
   return 16 + 2 * (int64_t)item_list_capacity(nkb);
+}
+
+// The item-order section of a mask buffer, after the tile lists: arrive and stamp (B * H words
+// each, padded to 16 bytes), then order (B * H * npairs words).
+__host__ __device__ inline int64_t order_words_padded(int64_t bh) { return (bh + 3) & ~int64_t(3); }
+__host__ __device__ inline int64_t order_section_bytes(int64_t bh, int64_t npairs) {
+  return 4 * (2 * order_words_padded(bh) + bh * npairs);
 }
 
 __device__ __forceinline__ uint32_t valid_bits32(int w, int nkb) {

@@ -13,7 +13,12 @@
 // the last mask word is the fused attention kernel's work counter; the pass zeroes it.  When a
 // list buffer is given the pass also builds every q-block pair's tile list for the fused kernel
 // (common.cuh: build_item_list) and writes the exact-block counts, so that no attention CTA
-// spends time on either between two items.
+// spends time on either between two items.  The last CTA of a head to finish its lists then
+// sorts the head's q-block pairs (after the sink pairs) by tile count, longest first, for the
+// fused kernel's work claims (AttnParams::order): handed out longest first within each head,
+// the last items of a launch are its shortest, which shortens the tail in which some CTAs
+// still run their last item while the others have none left.  Ties keep no fixed order; the
+// results do not depend on the order in which items run.
 #include "sm100.cuh"
 
 namespace solattn {
@@ -25,6 +30,80 @@ constexpr int kRouteThreads = 256;
 constexpr int kRowBytes = 144;                // staged centroid row (64 dims) + 16 bytes of skew
 constexpr int kStageBytes = 32 * kRowBytes;   // one warp's 32 rows
 constexpr int kRouteSmem = (kRouteThreads / 32) * 2 * kStageBytes;  // double-buffered, dynamic
+// The head sort reuses the staging memory: keys of up to kMaxOrderItems pairs and a histogram of
+// up to kMaxOrderBins tile counts (item_list_capacity(4096) + 1 = 4169 bins).  A head with more
+// pairs keeps the natural order.
+constexpr int kMaxOrderItems = 8192;
+constexpr int kMaxOrderBins = 4352;
+static_assert(4 * (kMaxOrderItems + kMaxOrderBins) <= kRouteSmem, "sort buffers exceed staging");
+
+// Block-wide exclusive scan of hist[0, bins) taken from the top bin down: afterwards hist[b]
+// holds the number of entries in bins above b (256 threads).
+__device__ __forceinline__ void scan_descending(int* hist, int bins, int* warp_sums) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int per = (bins + kRouteThreads - 1) / kRouteThreads;
+  const int r0 = t * per, r1 = min(bins, r0 + per);  // reversed positions r: bin bins - 1 - r
+  int local = 0;
+  for (int r = r0; r < r1; ++r) local += hist[bins - 1 - r];
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += warp_sums[w];
+  int run = before + incl - local;
+  for (int r = r0; r < r1; ++r) {
+    const int c = hist[bins - 1 - r];
+    hist[bins - 1 - r] = run;
+    run += c;
+  }
+}
+
+// Called by every thread of a routing CTA after its tile lists are written: the last CTA of the
+// head sorts the head's pairs and resets the head's arrival counter.
+__device__ __forceinline__ void order_head_items(const AttnParams& p, int bh, uint8_t* smem) {
+  __shared__ int s_last;
+  __shared__ int s_warp_sums[kRouteThreads / 32];
+  __threadfence();  // each writer's lists and headers are visible device-wide ...
+  __syncthreads();  // ... before the CTA counts itself in
+  if (threadIdx.x == 0) s_last = atomicAdd(p.arrive + bh, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // every other CTA's headers are visible
+  const int npairs = (p.nqb + 1) / 2;
+  const int sink = min(npairs, (p.q_sink_blocks + 1) / 2);
+  const int rest = npairs - sink;
+  const int bins = item_list_capacity(p.nkb) + 1;  // tile counts 0 .. capacity
+  if (rest > 0 && rest <= kMaxOrderItems && bins <= kMaxOrderBins) {
+    int* key = reinterpret_cast<int*>(smem);
+    int* hist = key + kMaxOrderItems;
+    const int64_t stride = item_list_stride(p.nkb);
+    const uint8_t* head = p.lists + (int64_t)bh * npairs * stride;
+    // Each key is read once (a stale header still yields a permutation of the pairs).
+    for (int i = threadIdx.x; i < rest; i += kRouteThreads)
+      key[i] = min(max(__ldcg(reinterpret_cast<const int*>(head + (int64_t)(sink + i) * stride)), 0),
+                   bins - 1);
+    for (int b = threadIdx.x; b < bins; b += kRouteThreads) hist[b] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < rest; i += kRouteThreads) atomicAdd(&hist[key[i]], 1);
+    __syncthreads();
+    scan_descending(hist, bins, s_warp_sums);
+    __syncthreads();
+    int32_t* order = p.order + (int64_t)bh * npairs;
+    for (int i = threadIdx.x; i < rest; i += kRouteThreads)
+      order[atomicAdd(&hist[key[i]], 1)] = sink + i;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      p.stamp[bh] = p.epoch;
+    }
+  }
+  if (threadIdx.x == 0) p.arrive[bh] = 0;  // every CTA of the head has arrived
+}
 
 template <int D>
 __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParams p) {
@@ -148,19 +227,21 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   // Warp j: the tile list of the group's q-block pair j (q-blocks qb_lo + 2j, qb_lo + 2j + 1).
   const int warp = threadIdx.x >> 5;
   const int qb0 = qb_lo + 2 * warp;
-  if (warp >= kRouteQB / 2 || qb0 >= p.nqb) return;
-  const bool has1 = qb0 + 1 < p.nqb;
-  uint8_t* item =
-      p.lists + ((int64_t)bh * ((p.nqb + 1) / 2) + (qb0 >> 1)) * item_list_stride(p.nkb);
-  int real;
-  const int n = build_item_list(smask[2 * warp], smask[2 * warp + 1], has1, nwords, nkb_b,
-                                p.force, reinterpret_cast<int16_t*>(item + 16), lane, real);
-  if (lane == 0) *reinterpret_cast<int4*>(item) = make_int4(n, real, 0, 0);
-  if (lane < 2 && p.counts && qb0 + lane < p.nqb) {
-    int c = 0;
-    for (int i = 0; i < nwords; ++i) c += __popc(smask[2 * warp + lane][i]);
-    p.counts[((int64_t)b * p.nqb + qb0 + lane) * p.H + bh % p.H] = c;
+  if (warp < kRouteQB / 2 && qb0 < p.nqb) {
+    const bool has1 = qb0 + 1 < p.nqb;
+    uint8_t* item =
+        p.lists + ((int64_t)bh * ((p.nqb + 1) / 2) + (qb0 >> 1)) * item_list_stride(p.nkb);
+    int real;
+    const int n = build_item_list(smask[2 * warp], smask[2 * warp + 1], has1, nwords, nkb_b,
+                                  p.force, reinterpret_cast<int16_t*>(item + 16), lane, real);
+    if (lane == 0) *reinterpret_cast<int4*>(item) = make_int4(n, real, 0, 0);
+    if (lane < 2 && p.counts && qb0 + lane < p.nqb) {
+      int c = 0;
+      for (int i = 0; i < nwords; ++i) c += __popc(smask[2 * warp + lane][i]);
+      p.counts[((int64_t)b * p.nqb + qb0 + lane) * p.H + bh % p.H] = c;
+    }
   }
+  if (p.arrive) order_head_items(p, bh, route_smem);
 }
 
 }  // namespace
