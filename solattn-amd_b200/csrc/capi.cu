@@ -113,10 +113,11 @@ Layout layout(int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D) {
   Layout L;
   const int64_t nqb = cdiv(Tq, kBlock), nkb = cdiv(Tk, kBlock);
   int64_t off = 0;
-  // The status word, then (at byte 16) the routing pass's per-head arrival counters, which
-  // solattn_sol_forward zeroes together with the status word before every call.
+  // The status word, then (at byte 16) two per-head counter arrays, the routing pass's and the
+  // pooling kernel's (finished K units), which solattn_sol_forward zeroes together with the
+  // status word before every call.
   L.status = off;
-  off = align256(off + 16 + 4 * B * H);
+  off = align256(off + 16 + 8 * B * H);
   L.kc = off;
   off = align256(off + B * H * nkb * D * 2);
   L.vc = off;
@@ -139,7 +140,8 @@ int pool_impl(const void* q, const void* k, const void* v, int64_t B, int64_t Tq
               int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH, int64_t k_sB,
               int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT, int64_t v_sH,
               const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows, int pool_q, float* qc,
-              void* kc, void* vc, const int32_t* key_counts, int32_t* status, void* stream);
+              void* kc, void* vc, const int32_t* key_counts, int32_t* status, int32_t* k_arrive,
+              float* mean, float* var, void* stream);
 
 // Rows of the underlying tensor addressed by a gather index (bounds for the device check).
 int64_t gather_rows(const int64_t* idx, int64_t idx_rows, int64_t T) { return idx ? idx_rows : T; }
@@ -191,7 +193,7 @@ int solattn_pool_qkv(const void* q, const void* k, const void* v, int64_t B, int
                      int64_t v_sH, const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows,
                      int pool_q, float* qc, void* kc, void* vc, int32_t* status, void* stream) {
   return pool_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT, v_sH,
-                   q_idx, kv_idx, idx_rows, pool_q, qc, kc, vc, nullptr, status, stream);
+                   q_idx, kv_idx, idx_rows, pool_q, qc, kc, vc, nullptr, status, nullptr, nullptr, nullptr, stream);
 }
 
 int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int64_t nqb,
@@ -214,7 +216,8 @@ int pool_impl(const void* q, const void* k, const void* v, int64_t B, int64_t Tq
               int64_t H, int64_t D, int64_t q_sB, int64_t q_sT, int64_t q_sH, int64_t k_sB,
               int64_t k_sT, int64_t k_sH, int64_t v_sB, int64_t v_sT, int64_t v_sH,
               const int64_t* q_idx, const int64_t* kv_idx, int64_t idx_rows, int pool_q, float* qc,
-              void* kc, void* vc, const int32_t* key_counts, int32_t* status, void* stream) {
+              void* kc, void* vc, const int32_t* key_counts, int32_t* status, int32_t* k_arrive,
+              float* mean, float* var, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (!k || !v || !kc || !vc || (pool_q && (!q || !qc))) return SOLATTN_ERR_ARG;
@@ -239,6 +242,9 @@ int pool_impl(const void* q, const void* k, const void* v, int64_t B, int64_t Tq
   p.B = (int)B;
   p.H = (int)H;
   p.tk_b = key_counts;
+  p.k_arrive = k_arrive;
+  p.mean = mean;
+  p.var = var;
   p.status = status;
   return from_cuda(launch_pool(p, (int)D, static_cast<cudaStream_t>(stream)));
 }
@@ -253,7 +259,8 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
                    const uint8_t* protect, float scale, int force, int local,
                    int kv_sink_blocks, int q_sink_blocks, void* out, const int64_t* out_idx,
                    int64_t out_rows, const int32_t* key_counts, int32_t* counts, int32_t* status,
-                   uint32_t* masks, int32_t* arrive, void* stream) {
+                   uint32_t* masks, int32_t* arrive, const float* mean, const float* var,
+                   float* cutoff_out, float beta, void* stream) {
   int rc = check_shapes(B, Tq, Tk, H, D);
   if (rc) return rc;
   if (!q || !k || !v || !kc || !vc || !out) return SOLATTN_ERR_ARG;
@@ -262,7 +269,8 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
   if (out_idx && out_rows <= 0) return SOLATTN_ERR_ARG;
   if (key_counts && !kv_idx) return SOLATTN_ERR_ARG;  // ragged key counts: indexed inputs only
   if ((q_idx || kv_idx) && idx_rows <= 0) return SOLATTN_ERR_ARG;
-  if (force < 0 || force > 2 || (force == 0 && (!qc || !cutoff))) return SOLATTN_ERR_ARG;
+  if (force < 0 || force > 2 || (force == 0 && (!qc || (!cutoff && !(mean && var)))))
+    return SOLATTN_ERR_ARG;
   if (!(scale > 0.f) || !isfinite(scale) || kv_sink_blocks < 0 || q_sink_blocks < 0)
     return SOLATTN_ERR_ARG;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(kc) ||
@@ -279,6 +287,10 @@ int attention_impl(const void* q, const void* k, const void* v, int64_t B, int64
   p.vc = static_cast<const __nv_bfloat16*>(vc);
   p.qc = qc;
   p.cutoff = cutoff;
+  p.mean = force == 0 ? mean : nullptr;
+  p.var = force == 0 ? var : nullptr;
+  p.cutoff_out = cutoff_out;
+  p.beta = beta;
   p.protect = protect;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_idx = out_idx;
@@ -338,29 +350,37 @@ int sol_forward_impl(const void* q, const void* k, const void* v, int64_t B, int
   void* vc = ws + L.vc;
   float* cutoff = reinterpret_cast<float*>(ws + L.cutoff);
   int32_t* status = reinterpret_cast<int32_t*>(ws + L.status);
-  // The status word and the routing pass's arrival counters (byte 16 on) in one memset.
-  if (cudaMemsetAsync(status, 0, (size_t)(16 + 4 * B * H), static_cast<cudaStream_t>(stream)) !=
+  int32_t* route_arrive = status + 4;             // byte 16
+  int32_t* k_arrive = route_arrive + B * H;       // the pooling kernel's finished K units
+  float* mean = reinterpret_cast<float*>(ws + L.mean);
+  float* var = reinterpret_cast<float*>(ws + L.var);
+  // The status word and both counter arrays in one memset.
+  if (cudaMemsetAsync(status, 0, (size_t)(16 + 8 * B * H), static_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
     return SOLATTN_ERR_CUDA;
+  const bool thr = force == SOLATTN_FORCE_THRESHOLD;
+  // Threshold mode on the tcgen05 path (up to 4096 key blocks, where the routing pass runs):
+  // the pooling kernel computes each head's key moments as its K units finish and the routing
+  // pass forms the cutoffs, so no threshold launch sits between pooling and routing.  The
+  // mma.sync kernel (more key blocks) routes in its own prologue from cutoffs computed first.
+  const bool fused = thr && nkb <= 4096;
   rc = pool_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT, v_sH,
-                 q_idx, kv_idx, idx_rows, force == SOLATTN_FORCE_THRESHOLD, qc, kc, vc, key_counts,
-                 status, stream);
+                 q_idx, kv_idx, idx_rows, thr, qc, kc, vc, key_counts, status,
+                 fused ? k_arrive : nullptr, mean, var, stream);
   if (rc) return rc;
-  if (force == SOLATTN_FORCE_THRESHOLD) {
+  if (thr && !fused) {
     rc = from_cuda(launch_threshold(static_cast<const __nv_bfloat16*>(kc), qc, (int)(B * H),
-                                    (int)H, (int)nqb, (int)nkb, (int)D, scale, beta,
-                                    reinterpret_cast<float*>(ws + L.mean),
-                                    reinterpret_cast<float*>(ws + L.var), cutoff, key_counts,
-                                    static_cast<cudaStream_t>(stream)));
+                                    (int)H, (int)nqb, (int)nkb, (int)D, scale, beta, mean, var,
+                                    cutoff, key_counts, static_cast<cudaStream_t>(stream)));
     if (rc) return rc;
   }
   return attention_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB,
-                        v_sT, v_sH, q_idx, kv_idx, idx_rows, kc, vc,
-                        force == SOLATTN_FORCE_THRESHOLD ? qc : nullptr,
-                        force == SOLATTN_FORCE_THRESHOLD ? cutoff : nullptr, protect, scale, force,
-                        local, kv_sink_blocks, q_sink_blocks, out, out_idx, out_rows, key_counts,
-                        counts, status, reinterpret_cast<uint32_t*>(ws + L.masks), status + 4,
-                        stream);
+                        v_sT, v_sH, q_idx, kv_idx, idx_rows, kc, vc, thr ? qc : nullptr,
+                        thr && !fused ? cutoff : nullptr, protect, scale, force, local,
+                        kv_sink_blocks, q_sink_blocks, out, out_idx, out_rows, key_counts, counts,
+                        status, reinterpret_cast<uint32_t*>(ws + L.masks), route_arrive,
+                        fused ? mean : nullptr, fused ? var : nullptr, fused ? cutoff : nullptr,
+                        beta, stream);
 }
 
 }  // namespace
@@ -378,7 +398,7 @@ int solattn_attention(const void* q, const void* k, const void* v, int64_t B, in
   return attention_impl(q, k, v, B, Tq, Tk, H, D, q_sB, q_sT, q_sH, k_sB, k_sT, k_sH, v_sB, v_sT,
                         v_sH, q_idx, kv_idx, idx_rows, kc, vc, qc, cutoff, protect, scale, force,
                         local, kv_sink_blocks, q_sink_blocks, out, nullptr, 0, nullptr, counts,
-                        status, masks, nullptr, stream);
+                        status, masks, nullptr, nullptr, nullptr, nullptr, 0.f, stream);
 }
 
 int solattn_sol_forward(const void* q, const void* k, const void* v, int64_t B, int64_t Tq,
@@ -435,7 +455,7 @@ int solattn_dense_rows(const void* q, const void* k, const void* v, const int64_
   return attention_impl(q, k, v, 1, n_rows, N, H, D, 0, q_sT, q_sH, 0, k_sT, k_sH, 0, v_sT, v_sH,
                         rows, nullptr, N, k, v, nullptr, nullptr, nullptr, scale,
                         SOLATTN_FORCE_ALL, -1, 0, 0, out, rows, N, nullptr, nullptr, status,
-                        nullptr, nullptr, stream);
+                        nullptr, nullptr, nullptr, nullptr, nullptr, 0.f, stream);
 }
 
 int solattn_dense(const void* q, const void* k, const void* v, int64_t B, int64_t Tq, int64_t Tk,

@@ -29,7 +29,13 @@ struct AttnParams {
   const __nv_bfloat16* kc;  // [B, H, nkb, D]
   const __nv_bfloat16* vc;  // [B, H, nkb, D]
   const float* qc;          // [B, H, nqb, D]
-  const float* cutoff;      // [B, H, nqb]
+  const float* cutoff;      // [B, H, nqb] (read by routing unless mean/var are given)
+  // The full forward's fused threshold: the pooling kernel wrote the key moments mean / var
+  // [B, H, D], and each routing CTA forms its q-blocks' cutoffs from them (threshold.cuh
+  // arithmetic) and writes them to cutoff_out [B, H, nqb]; else nullptr.
+  const float* mean;
+  const float* var;
+  float* cutoff_out;
   const uint8_t* protect;   // [B, nqb, nkb] or nullptr
   __nv_bfloat16* out;       // [B, Tq, H, D], or NHD [out_rows, H, D] when out_idx is set
   const int64_t* out_idx;   // optional output rows [B, Tq]: row t of batch b goes to
@@ -55,6 +61,7 @@ struct AttnParams {
   const int32_t* tk_b;  // optional per-batch key counts [B] (ragged indexed plans: batch b has
                         // tk_b[b] <= Tk keys, ceil(tk_b[b] / 64) key blocks), else nullptr
   float scale;       // softmax scale (natural-log units), used by routing
+  float beta;        // Eq. 15 beta (the fused threshold's cutoffs)
   float scale_log2;  // scale * log2(e), used by the softmax
   int force, local, kv_sink_blocks, q_sink_blocks;
 };
@@ -67,6 +74,13 @@ struct PoolParams {
   const int32_t* tk_b;  // optional per-batch key counts [B] for K and V (ragged), else nullptr
   void* y[3];        // qc (float), kc (bf16), vc (bf16)
   int B, H;
+  int order[3];      // tensor of grid row y (set by the launcher: K, then Q, then V)
+  // Fused key moments (the full forward in threshold mode, else nullptr): k_arrive[B * H]
+  // counts the finished K units of each head (zero at the start of the launch); the CTA that
+  // finishes a head's last K unit computes the head's mean / var [B, H, D] (threshold.cuh).
+  int32_t* k_arrive;
+  float* mean;
+  float* var;
   int32_t* status;
 };
 

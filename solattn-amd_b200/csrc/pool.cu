@@ -10,34 +10,38 @@
 //
 // The pass is HBM-bound: it reads every Q/K/V element once (the 64 rows of a unit are
 // strided by sT, each row a contiguous 2*D-byte segment) and writes 1/64 of that back.
-#include "sm100.cuh"
+#include "threshold.cuh"
 
 namespace solattn {
 
-template <int D>
-__global__ void __launch_bounds__(256) pool_kernel(PoolParams p) {
+template <int D, bool kGather>
+__global__ void __launch_bounds__(256, 4) pool_kernel(PoolParams p) {
   constexpr int kChunks = D / 8;          // 16-byte chunks per row
   constexpr int kUnitsPerCta = 256 / D;   // D threads per unit
   __shared__ float part[kUnitsPerCta][8][D];
 
+  const int which = p.order[blockIdx.y];  // 0: Q, 1: K, 2: V (uniform per CTA)
   const int local_unit = threadIdx.x / D;
   const int lt = threadIdx.x % D;
   const int g = lt / kChunks;  // row group 0..7
   const int c = lt % kChunks;  // chunk lane
 
-  int64_t unit = (int64_t)blockIdx.x * kUnitsPerCta + local_unit;
-  int which = 0;
-  while (which < 3 && unit >= p.units[which]) {
-    unit -= p.units[which];
-    ++which;
-  }
-  const bool active = which < 3;
+  const int64_t unit = (int64_t)blockIdx.x * kUnitsPerCta + local_unit;
+  const bool active = unit < p.units[which];
   int b = 0, blk = 0, h = 0, n = 0;
   // Sums of channels (2j, 2j + 1) in packed f32x2 pairs: each lane of add.rn.f32x2 rounds like
   // __fadd_rn, so the sums are those of the scalar order with half the adds.
   uint64_t acc2[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) acc2[j] = 0ull;
+  auto add_row = [&](const uint4& raw) {
+    const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(v2[j]);
+      acc2[j] = sm100::f2_add(acc2[j], sm100::f2_pack(f.x, f.y));
+    }
+  };
   if (active) {
     const TensorView& x = p.x[which];
     const int T = p.T[which];
@@ -51,57 +55,114 @@ __global__ void __launch_bounds__(256) pool_kernel(PoolParams p) {
                                          : T;  // valid rows of this batch
     n = min(kBlock, Tv - blk * kBlock);
     uint4 raw[8];
+    if constexpr (!kGather) {
+      // Rows g, g + 8, ... of the block are one stride apart: one base address, no per-row
+      // index arithmetic (the kernel is bound by instruction issue, not by its loads).
+      const __nv_bfloat16* base = x.ptr + (int64_t)b * x.sB +
+                                  (int64_t)(blk * kBlock + g) * x.sT + (int64_t)h * x.sH + c * 8;
+      const int64_t step = 8 * x.sT;
+      if (n == kBlock) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int row = g + 8 * i;
-      if (row < n) {
-        const __nv_bfloat16* src = row_ptr(x, T, b, h, blk * kBlock + row, p.status) + c * 8;
-        raw[i] = __ldg(reinterpret_cast<const uint4*>(src));
+        for (int i = 0; i < 8; ++i) raw[i] = __ldg(reinterpret_cast<const uint4*>(base + i * step));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) add_row(raw[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (g + 8 * i < n) raw[i] = __ldg(reinterpret_cast<const uint4*>(base + i * step));
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (g + 8 * i < n) add_row(raw[i]);
       }
-    }
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int row = g + 8 * i;
-      if (row < n) {
-        const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(v2[j]);
-          acc2[j] = sm100::f2_add(acc2[j], sm100::f2_pack(f.x, f.y));
+      for (int i = 0; i < 8; ++i) {
+        const int row = g + 8 * i;
+        if (row < n) {
+          const __nv_bfloat16* src = row_ptr(x, T, b, h, blk * kBlock + row, p.status) + c * 8;
+          raw[i] = __ldg(reinterpret_cast<const uint4*>(src));
         }
       }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (g + 8 * i < n) add_row(raw[i]);
     }
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j)
     sm100::f2_unpack(acc2[j], part[local_unit][g][c * 8 + 2 * j], part[local_unit][g][c * 8 + 2 * j + 1]);
   __syncthreads();
-  if (!active) return;
-  // Thread lt now owns channel lt of the unit.
-  float s = 0.f;
+  if (active) {
+    // Thread lt now owns channel lt of the unit.
+    float s = 0.f;
 #pragma unroll
-  for (int gg = 0; gg < 8; ++gg) s = __fadd_rn(s, part[local_unit][gg][lt]);
-  const float mean = n > 0 ? __fdiv_rn(s, (float)n) : 0.f;
-  const int nb = p.nb[which];
-  const int64_t o = (((int64_t)b * p.H + h) * nb + blk) * D + lt;
-  if (which == 0) {
-    reinterpret_cast<float*>(p.y[0])[o] = mean;
-  } else {
-    reinterpret_cast<__nv_bfloat16*>(p.y[which])[o] = __float2bfloat16_rn(mean);
+    for (int gg = 0; gg < 8; ++gg) s = __fadd_rn(s, part[local_unit][gg][lt]);
+    const float mean = n > 0 ? __fdiv_rn(s, (float)n) : 0.f;
+    const int nb = p.nb[which];
+    const int64_t o = (((int64_t)b * p.H + h) * nb + blk) * D + lt;
+    if (which == 0) {
+      reinterpret_cast<float*>(p.y[0])[o] = mean;
+    } else {
+      reinterpret_cast<__nv_bfloat16*>(p.y[which])[o] = __float2bfloat16_rn(mean);
+    }
+  }
+  if (!p.k_arrive || which != 1) return;  // uniform: moments are fused for K CTAs only
+  // The CTA that finishes the last K unit of a head computes the head's key moments
+  // (threshold.cuh) while the V units are still being pooled.
+  __shared__ int s_head[kUnitsPerCta];
+  __shared__ float s_mean[D];
+  __shared__ float s_var[D];
+  __threadfence();  // this unit's centroid row is visible device-wide ...
+  __syncthreads();  // ... before the unit is counted
+  if (lt == 0) {
+    int head = -1;
+    if (active) {
+      const int bh = b * p.H + h;
+      if (atomicAdd(p.k_arrive + bh, 1) == p.nb[1] - 1) head = bh;
+    }
+    s_head[local_unit] = head;
+  }
+  __syncthreads();
+  // The shape [2][kThrSlices][D] of the moment partials fits in the unit partials' storage.
+  static_assert(sizeof(part) >= sizeof(float) * 2 * kThrSlices * D, "moment partials");
+  auto* s_part = reinterpret_cast<float (*)[kThrSlices][D]>(&part[0][0][0]);
+  for (int u = 0; u < kUnitsPerCta; ++u) {
+    const int bh = s_head[u];
+    if (bh < 0) continue;
+    __threadfence();  // every other CTA's rows of the head are visible
+    const int nkb = p.nb[1];
+    const int tk = p.tk_b ? clamp_key_count(__ldg(p.tk_b + bh / p.H), p.T[1], p.status) : p.T[1];
+    const int nbk = min(max((tk + kBlock - 1) / kBlock, 1), nkb);
+    head_moments<D, 256>(reinterpret_cast<const __nv_bfloat16*>(p.y[1]) + (int64_t)bh * nkb * D,
+                         nbk, s_part, s_mean, s_var, p.mean + (int64_t)bh * D,
+                         p.var + (int64_t)bh * D);
   }
 }
 
 cudaError_t launch_pool(const PoolParams& p, int D, cudaStream_t stream) {
-  const int64_t total = p.units[0] + p.units[1] + p.units[2];
-  if (total == 0) return cudaSuccess;
-  for (int i = 0; i < 3; ++i)
+  int64_t most = 0;
+  for (int i = 0; i < 3; ++i) {
     if (p.units[i] > 0x7fffffff) return cudaErrorInvalidValue;  // 32-bit unit decode
+    most = p.units[i] > most ? p.units[i] : most;
+  }
+  if (most == 0) return cudaSuccess;
   const int per_cta = 256 / D;
-  const int64_t grid = (total + per_cta - 1) / per_cta;
-  if (D == 128)
-    pool_kernel<128><<<(unsigned)grid, 256, 0, stream>>>(p);
-  else
-    pool_kernel<64><<<(unsigned)grid, 256, 0, stream>>>(p);
+  // x: units of one tensor; y: the tensors pooled, K first (CTAs past a tensor's units return
+  // at once).  Grid rows are dispatched in order, so with the key moments fused the last K
+  // units -- and the moments they start -- overlap the Q and V rows.
+  PoolParams q = p;
+  int rows = 0;
+  for (int t : {1, 0, 2})
+    if (p.units[t] > 0) q.order[rows++] = t;
+  const dim3 grid((unsigned)((most + per_cta - 1) / per_cta), (unsigned)rows);
+  const bool gather = p.x[0].idx || p.x[1].idx || p.x[2].idx;
+  if (D == 128) {
+    if (gather) pool_kernel<128, true><<<grid, 256, 0, stream>>>(q);
+    else pool_kernel<128, false><<<grid, 256, 0, stream>>>(q);
+  } else {
+    if (gather) pool_kernel<64, true><<<grid, 256, 0, stream>>>(q);
+    else pool_kernel<64, false><<<grid, 256, 0, stream>>>(q);
+  }
   return cudaGetLastError();
 }
 

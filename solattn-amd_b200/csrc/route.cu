@@ -19,7 +19,7 @@
 // the last items of a launch are its shortest, which shortens the tail in which some CTAs
 // still run their last item while the others have none left.  Ties keep no fixed order; the
 // results do not depend on the order in which items run.
-#include "sm100.cuh"
+#include "threshold.cuh"
 
 namespace solattn {
 
@@ -124,10 +124,21 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
     sq[j][i % D] =
         (p.force == 0 && j < nq) ? p.qc[((int64_t)bh * p.nqb + qb_lo + j) * D + (i % D)] : 0.f;
   }
-  if (threadIdx.x < kRouteQB)
+  // Threshold mode reads the cutoffs, or (fused threshold) forms them below from the key
+  // moments staged here.
+  const bool fused_cut = p.force == 0 && p.mean != nullptr;
+  __shared__ float s_mean[D];
+  __shared__ float s_var[D];
+  if (fused_cut) {
+    for (int d = threadIdx.x; d < D; d += kRouteThreads) {
+      s_mean[d] = p.mean[(int64_t)bh * D + d];
+      s_var[d] = p.var[(int64_t)bh * D + d];
+    }
+  } else if (threadIdx.x < kRouteQB) {
     scut[threadIdx.x] = (p.force == 0 && (int)threadIdx.x < nq)
                             ? p.cutoff[(int64_t)bh * p.nqb + qb_lo + threadIdx.x]
                             : 0.f;
+  }
   __syncthreads();
 
   // Per-warp staging of its 32 centroid rows, 64 dims at a time, double-buffered: the 16-byte
@@ -157,6 +168,24 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
     cp_async_commit();
   };
   issue(0);
+  // The cutoffs this warp compares against, in registers.  Fused threshold: every warp forms
+  // the group's four cutoffs itself (eight lanes per q-block, threshold.cuh) while its first
+  // centroid chunk is in flight, so that no warp waits for another.
+  float cut[kRouteQB];
+  if (fused_cut) {
+    static_assert(kRouteQB * kThrSlices == 32, "one warp forms the group's cutoffs");
+    const int j = lane / kThrSlices;
+    const bool valid = j < nq;
+    const float c = qblock_cutoff<D>(p.qc + ((int64_t)bh * p.nqb + qb_lo + (valid ? j : 0)) * D,
+                                     s_mean, s_var, valid, p.scale, p.beta);
+#pragma unroll
+    for (int i = 0; i < kRouteQB; ++i) cut[i] = __shfl_sync(0xffffffffu, c, kThrSlices * i);
+    if (warp_id == 0 && valid && lane % kThrSlices == 0 && p.cutoff_out)
+      p.cutoff_out[(int64_t)bh * p.nqb + qb_lo + j] = c;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kRouteQB; ++i) cut[i] = scut[i];
+  }
   int t = 0;
   // Warp-uniform loop over 32-block words.
   for (int w = warp_id; w < nwords; w += kRouteThreads / 32) {
@@ -213,7 +242,7 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
                                   __fadd_rn(__fadd_rn(part[4], part[5]),
                                             __fadd_rn(part[6], part[7])));
       bool sel = false;
-      if (kb < nkb_b) sel = route_rules(p, p.force == 0 && __fmul_rn(dot, p.scale) > scut[j], b, qb, kb);
+      if (kb < nkb_b) sel = route_rules(p, p.force == 0 && __fmul_rn(dot, p.scale) > cut[j], b, qb, kb);
       const uint32_t bal = __ballot_sync(0xffffffffu, sel);
       if (lane == 0) {
         p.masks[((int64_t)bh * p.nqb + qb) * nwords + w] = bal;
