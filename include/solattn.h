@@ -63,9 +63,11 @@ SOLATTN_API const char* solattn_strerror(int code);
 /*
  * Scratch layout of one forward call.  Replaces the torch.empty allocations of the
  * reference launcher (kernels.py:185-190, 203-217): kc/vc (BF16 K/V block means), qc (FP32
- * Q block means), mean/var (FP32 key moments), cutoff (FP32 Eq. 15 thresholds), one device
- * status word, and masks (solattn_masks_bytes(): the routing decisions, uint32 bitmask
- * [B, H, nqb, ceil(nkb/32)], then the fused kernel's work counter and per-item tile lists).
+ * Q block means), mean/var (FP32 key moments), cutoff (FP32 Eq. 15 thresholds), the status
+ * section (one device status word at its start, then at byte 16 two int32 [B * H] counter
+ * arrays that solattn_sol_forward zeroes together with the status word), and masks
+ * (solattn_masks_bytes(): the routing decisions, uint32 bitmask [B, H, nqb, ceil(nkb/32)],
+ * then the fused kernel's work counter, per-item tile lists and item order).
  * Offsets are in bytes from the workspace base, each 256-byte aligned.  The pooled tensors
  * use the layout [B, H, blocks, D]; cutoff is [B, H, nqb].
  * Returns the total size in bytes, or 0 on an invalid shape.
@@ -94,15 +96,18 @@ SOLATTN_API int solattn_pool_qkv(const void* q, const void* k, const void* v,
                      float* qc, void* kc, void* vc, int32_t* status, void* stream);
 
 /*
- * Key moments and Eq. 15 thresholds.  Replaces `_moments` + `_threshold`
+ * Key moments and Eq. 15 thresholds (the stage-by-stage form; solattn_sol_forward computes
+ * the same bits inside its pooling and routing launches).  Replaces `_moments` + `_threshold`
  * (kernels.py:30-64, launches 211-215): per (b, h, d) mean = sum(kc)/nkb and
- * var = max(sum(kc^2)/nkb - mean^2, 0) over all key blocks, unweighted (sequential FP32
- * sums over blocks); per (b, h, q-block)
- * cutoff = (sum_d qc*mean + beta * sqrt(sum_d (qc*qc)*var)) * scale with sequential FP32
- * sums over d.  The cutoff is in natural-log units: the attention kernel selects key block j
- * iff dot * scale > cutoff, where dot = sum_d qc[d]*kc_j[d] taken as eight partial sums
- * p_j over d = 8i + j combined as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); every operation is
- * rounded to nearest FP32, no fused multiply-add.  beta must be finite.
+ * var = max(sum(kc^2)/nkb - mean^2, 0) over all key blocks, unweighted, each sum taken as
+ * eight slice sums s_j over blocks j, j+8, j+16, ... (in order) combined as
+ * ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)); per (b, h, q-block)
+ * cutoff = (sum_d qc*mean + beta * sqrt(sum_d (qc*qc)*var)) * scale, each sum over d taken
+ * as eight partial sums over d = 8i + e combined in the same tree.  The cutoff is in
+ * natural-log units: the attention kernel selects key block j iff dot * scale > cutoff,
+ * where dot = sum_d qc[d]*kc_j[d] taken as eight partial sums p_j over d = 8i + j combined
+ * as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); every operation is rounded to nearest FP32, no
+ * fused multiply-add.  beta must be finite.
  */
 SOLATTN_API int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int64_t nqb,
                       int64_t nkb, int64_t D, float scale, float beta, float* mean, float* var,
@@ -124,9 +129,13 @@ SOLATTN_API int64_t solattn_masks_bytes(int64_t B, int64_t Tq, int64_t Tk, int64
  * and the attention kernel reads it back.  The buffer (16-byte aligned) holds
  * solattn_masks_bytes(B, Tq, Tk, H) bytes: the bitmask, then the attention kernel's work
  * counter (zeroed by the routing pass, then incremented as the persistent CTAs take work
- * items) and one tile list per q-block pair (built by the routing pass).  It is required when
- * force == SOLATTN_FORCE_THRESHOLD and may be NULL in the force modes (the rules are then
- * evaluated inside the kernel and the work is split round robin).
+ * items), one tile list per q-block pair (built by the routing pass), and the item order:
+ * per head a counter of routing CTAs, a stamp and the head's q-block pairs sorted by tile
+ * count (the attention kernel hands items out longest first within each head).  The
+ * counters must be zero before a buffer's first use (a zero-filled buffer); every call leaves
+ * them zero.  It is required when force == SOLATTN_FORCE_THRESHOLD and may be NULL in the
+ * force modes (the rules are then evaluated inside the kernel and the work is split round
+ * robin).
  */
 SOLATTN_API int solattn_attention(const void* q, const void* k, const void* v,
                       int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,
@@ -140,9 +149,13 @@ SOLATTN_API int solattn_attention(const void* q, const void* k, const void* v,
                       int32_t* status, uint32_t* masks, void* stream);
 
 /*
- * All-in SOL forward: pool -> threshold (force == 0 only) -> fused attention, the whole of
- * `launch_sol` (kernels.py:203-225), using the caller's workspace of
- * solattn_workspace_layout() bytes.  beta may be +-inf (selects the force mode) but not NaN.
+ * All-in SOL forward, the whole of `launch_sol` (kernels.py:203-225), using the caller's
+ * workspace of solattn_workspace_layout() bytes: pooling (which, for force == 0, also
+ * computes each head's key moments as its last K unit finishes), the routing pass (which
+ * forms the cutoffs of its q-blocks from them), then the fused attention; the moments,
+ * cutoffs and routing are bit-identical to solattn_threshold + solattn_attention.  With more
+ * than 4096 key blocks the threshold kernel runs between pooling and attention instead.
+ * beta may be +-inf (selects the force mode) but not NaN.
  */
 SOLATTN_API int solattn_sol_forward(const void* q, const void* k, const void* v,
                         int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D,

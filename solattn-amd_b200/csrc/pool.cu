@@ -26,8 +26,15 @@ __global__ void __launch_bounds__(256, 4) pool_kernel(PoolParams p) {
   const int g = lt / kChunks;  // row group 0..7
   const int c = lt % kChunks;  // chunk lane
 
-  const int64_t unit = (int64_t)blockIdx.x * kUnitsPerCta + local_unit;
-  const bool active = unit < p.units[which];
+  // A CTA takes kUnitsPerCta consecutive blocks of one (b, h); consecutive CTAs take the next
+  // head of the same rows (DRAM rows are read whole across a wave of CTAs), and with fused
+  // moments the CTA finishing a head's last K block computes that head alone.
+  const int nb_t = p.nb[which];
+  const int groups = (nb_t + kUnitsPerCta - 1) / kUnitsPerCta;  // block groups per (b, h)
+  const int cta = (int)blockIdx.x;  // < B * H * groups (the launcher checks 32 bits)
+  const int hh = cta % p.H, rr = cta / p.H;
+  const int bb = rr / groups, blk0 = (rr % groups) * kUnitsPerCta;
+  const bool active = bb < p.B && blk0 + local_unit < nb_t && p.units[which] > 0;
   int b = 0, blk = 0, h = 0, n = 0;
   // Sums of channels (2j, 2j + 1) in packed f32x2 pairs: each lane of add.rn.f32x2 rounds like
   // __fadd_rn, so the sums are those of the scalar order with half the adds.
@@ -45,12 +52,9 @@ __global__ void __launch_bounds__(256, 4) pool_kernel(PoolParams p) {
   if (active) {
     const TensorView& x = p.x[which];
     const int T = p.T[which];
-    // Unit indices fit 32 bits (the launcher checks), so the decode uses 32-bit division.
-    const int u32 = (int)unit;
-    h = u32 % p.H;
-    const int r = u32 / p.H;
-    blk = r % p.nb[which];
-    b = r / p.nb[which];
+    h = hh;
+    b = bb;
+    blk = blk0 + local_unit;
     const int Tv = (which > 0 && p.tk_b) ? clamp_key_count(__ldg(p.tk_b + b), T, p.status)
                                          : T;  // valid rows of this batch
     n = min(kBlock, Tv - blk * kBlock);
@@ -109,26 +113,31 @@ __global__ void __launch_bounds__(256, 4) pool_kernel(PoolParams p) {
   if (!p.k_arrive || which != 1) return;  // uniform: moments are fused for K CTAs only
   // The CTA that finishes the last K unit of a head computes the head's key moments
   // (threshold.cuh) while the V units are still being pooled.
-  __shared__ int s_head[kUnitsPerCta];
+  __shared__ int s_head[1];
   __shared__ float s_mean[D];
   __shared__ float s_var[D];
-  __threadfence();  // this unit's centroid row is visible device-wide ...
-  __syncthreads();  // ... before the unit is counted
-  if (lt == 0) {
+  // The CTA's rows are written (barrier), then one thread makes them visible device-wide
+  // (a cumulative fence) and counts the CTA's blocks in; a fence in every thread would hold
+  // each K CTA until all of its stores had drained.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int n_active = 0;
+    for (int u = 0; u < kUnitsPerCta; ++u) n_active += (blk0 + u < nb_t) ? 1 : 0;
     int head = -1;
-    if (active) {
-      const int bh = b * p.H + h;
-      if (atomicAdd(p.k_arrive + bh, 1) == p.nb[1] - 1) head = bh;
+    if (bb < p.B) {
+      const int bh = bb * p.H + hh;
+      __threadfence();
+      if (atomicAdd(p.k_arrive + bh, n_active) + n_active == p.nb[1]) head = bh;
     }
-    s_head[local_unit] = head;
+    s_head[0] = head;
   }
   __syncthreads();
   // The shape [2][kThrSlices][D] of the moment partials fits in the unit partials' storage.
   static_assert(sizeof(part) >= sizeof(float) * 2 * kThrSlices * D, "moment partials");
   auto* s_part = reinterpret_cast<float (*)[kThrSlices][D]>(&part[0][0][0]);
-  for (int u = 0; u < kUnitsPerCta; ++u) {
-    const int bh = s_head[u];
-    if (bh < 0) continue;
+  {
+    const int bh = s_head[0];
+    if (bh < 0) return;
     __threadfence();  // every other CTA's rows of the head are visible
     const int nkb = p.nb[1];
     const int tk = p.tk_b ? clamp_key_count(__ldg(p.tk_b + bh / p.H), p.T[1], p.status) : p.T[1];
@@ -140,21 +149,23 @@ __global__ void __launch_bounds__(256, 4) pool_kernel(PoolParams p) {
 }
 
 cudaError_t launch_pool(const PoolParams& p, int D, cudaStream_t stream) {
-  int64_t most = 0;
-  for (int i = 0; i < 3; ++i) {
-    if (p.units[i] > 0x7fffffff) return cudaErrorInvalidValue;  // 32-bit unit decode
-    most = p.units[i] > most ? p.units[i] : most;
-  }
-  if (most == 0) return cudaSuccess;
   const int per_cta = 256 / D;
-  // x: units of one tensor; y: the tensors pooled, K first (CTAs past a tensor's units return
-  // at once).  Grid rows are dispatched in order, so with the key moments fused the last K
-  // units -- and the moments they start -- overlap the Q and V rows.
+  // x: CTAs of one tensor (per_cta consecutive blocks of one head each); y: the tensors pooled,
+  // K first (CTAs past a tensor's blocks return at once).  Grid rows are dispatched in order,
+  // so with the key moments fused the last K blocks -- and the moments they start -- overlap
+  // the Q and V rows.
   PoolParams q = p;
   int rows = 0;
-  for (int t : {1, 0, 2})
-    if (p.units[t] > 0) q.order[rows++] = t;
-  const dim3 grid((unsigned)((most + per_cta - 1) / per_cta), (unsigned)rows);
+  int64_t most = 0;
+  for (int t : {1, 0, 2}) {
+    if (p.units[t] <= 0) continue;
+    q.order[rows++] = t;
+    const int64_t ctas = (int64_t)p.B * p.H * ((p.nb[t] + per_cta - 1) / per_cta);
+    if (ctas > 0x7fffffff) return cudaErrorInvalidValue;  // 32-bit CTA decode
+    most = ctas > most ? ctas : most;
+  }
+  if (rows == 0) return cudaSuccess;
+  const dim3 grid((unsigned)most, (unsigned)rows);
   const bool gather = p.x[0].idx || p.x[1].idx || p.x[2].idx;
   if (D == 128) {
     if (gather) pool_kernel<128, true><<<grid, 256, 0, stream>>>(q);

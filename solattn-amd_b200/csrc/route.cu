@@ -68,9 +68,12 @@ __device__ __forceinline__ void scan_descending(int* hist, int bins, int* warp_s
 __device__ __forceinline__ void order_head_items(const AttnParams& p, int bh, uint8_t* smem) {
   __shared__ int s_last;
   __shared__ int s_warp_sums[kRouteThreads / 32];
-  __threadfence();  // each writer's lists and headers are visible device-wide ...
-  __syncthreads();  // ... before the CTA counts itself in
-  if (threadIdx.x == 0) s_last = atomicAdd(p.arrive + bh, 1) == (int)gridDim.x - 1;
+  __syncthreads();  // this CTA's lists and headers are written; one thread makes them visible
+                    // device-wide (a cumulative fence) before the CTA counts itself in
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(p.arrive + bh, 1) == (int)gridDim.x - 1;
+  }
   __syncthreads();
   if (!s_last) return;
   __threadfence();  // every other CTA's headers are visible
@@ -169,15 +172,16 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   };
   issue(0);
   // The cutoffs this warp compares against, in registers.  Fused threshold: every warp forms
-  // the group's four cutoffs itself (eight lanes per q-block, threshold.cuh) while its first
-  // centroid chunk is in flight, so that no warp waits for another.
+  // the group's four cutoffs itself from the q-block means already staged in shared memory
+  // (eight lanes per q-block, threshold.cuh) while its first centroid chunk is in flight, so
+  // that no warp waits for another.
   float cut[kRouteQB];
   if (fused_cut) {
     static_assert(kRouteQB * kThrSlices == 32, "one warp forms the group's cutoffs");
     const int j = lane / kThrSlices;
     const bool valid = j < nq;
-    const float c = qblock_cutoff<D>(p.qc + ((int64_t)bh * p.nqb + qb_lo + (valid ? j : 0)) * D,
-                                     s_mean, s_var, valid, p.scale, p.beta);
+    const float c = qblock_cutoff<D, true>(&sq[valid ? j : 0][0], s_mean, s_var, valid, p.scale,
+                                           p.beta);
 #pragma unroll
     for (int i = 0; i < kRouteQB; ++i) cut[i] = __shfl_sync(0xffffffffu, c, kThrSlices * i);
     if (warp_id == 0 && valid && lane % kThrSlices == 0 && p.cutoff_out)

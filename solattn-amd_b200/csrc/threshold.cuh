@@ -95,10 +95,11 @@ __device__ __forceinline__ void head_moments(const __nv_bfloat16* kc_bh, int nb,
   __syncthreads();
 }
 
-// The cutoff of the q-block whose means start at qrow, from the eight lanes e = lane % 8 of an
-// aligned lane octet (all 32 lanes of the warp must call it; `valid` false gives a lane zero
-// partial sums, and its octet's result is not used).
-template <int D>
+// The cutoff of the q-block whose means start at qrow (global memory, or shared memory when
+// kSharedRow), from the eight lanes e = lane % 8 of an aligned lane octet (all 32 lanes of the
+// warp must call it; `valid` false gives a lane zero partial sums, and its octet's result is
+// not used).
+template <int D, bool kSharedRow = false>
 __device__ __forceinline__ float qblock_cutoff(const float* qrow, const float* s_mean,
                                                const float* s_var, bool valid, float scale,
                                                float beta) {
@@ -107,7 +108,8 @@ __device__ __forceinline__ float qblock_cutoff(const float* qrow, const float* s
   if (valid) {
     float qv[D / kThrSlices];
 #pragma unroll
-    for (int i = 0; i < D / kThrSlices; ++i) qv[i] = __ldcg(qrow + kThrSlices * i + e);
+    for (int i = 0; i < D / kThrSlices; ++i)
+      qv[i] = kSharedRow ? qrow[kThrSlices * i + e] : __ldcg(qrow + kThrSlices * i + e);
 #pragma unroll
     for (int i = 0; i < D / kThrSlices; ++i) {
       const int d = kThrSlices * i + e;
