@@ -1,4 +1,5 @@
-"""Benchmark of the SOL routed-attention hot path (pool -> threshold -> fused attention).
+"""Benchmark of the SOL routed-attention hot path (pooling with key moments -> routing with
+cutoffs -> fused attention).
 
 Workload (the headline metric's configuration): video-DiT self-attention B=1, T=32768, H=24, D=128 BF16,
 block-smooth with drift (sigma=0.3), beta=1.0, kv/query sinks 128/128, local_blocks=1,
@@ -7,15 +8,24 @@ N ranks (one process per GPU, torchrun); there is no collective on the hot path:
 reduces the per-rank timings and gathers exact-block counts after the timed region.
 
 One JSON line on rank 0:
-  value        dense-equivalent TFLOPS of the whole job (4*B*H*Tq*Tk*D / max-over-ranks ms)
-  ms_per_step  max over ranks of the mean device time of one call (inputs resident in HBM)
-  e2e          the same metric through the public API from pinned host buffers, with the
-               host->device copies of Q/K/V and the device->host copy of the output timed
-  roofline     the fused attention kernel against the measured BF16 tensor peak
-  cpu_baseline the CPU oracle port timed on a bounded sample (rank 0, N=1)
+  value          dense-equivalent TFLOPS of the whole job (4*B*H*Tq*Tk*D / max-over-ranks ms)
+  ms_per_step    max over ranks of the mean device time of one call (inputs resident in HBM,
+                 L2 flushed between calls)
+  kernel_ms      the same kernels stage by stage (pool, threshold in its stage form, attention =
+                 routing pass + fused kernel); the public call folds the threshold into pooling
+                 and routing
+  roofline       the attention stage against the measured BF16 tensor peak; pool_roofline the
+                 pooling kernel against the measured HBM copy bandwidth
+  err            three whole heads (all q-blocks) against the CPU oracle port: outputs under the
+                 north-star gate and exact-block counts compared one by one
+  e2e            the same metric through the public host-buffer API (sol_attention_host), with
+                 the host->device copies of Q/K/V and the device->host copy of the output timed
+  c5             the indexed-window configuration (one ragged IndexedPlan of 64 windows,
+                 window-sharded under torchrun; plan creation and transfer timed apart)
+  cpu_baseline   the CPU oracle port on the heads of `err`, timed one by one (rank 0, N=1)
 
-``--impl reference`` times the CPU oracle port (the reference's FP32 Torch oracle
-restated in oracle/sol_oracle.py) on the host cores instead; only rank 0 works.
+``--impl reference`` times the CPU oracle port (the reference's FP32 Torch oracle restated in
+oracle/sol_oracle.py) on the host cores instead, one whole head per step; only rank 0 works.
 """
 
 from __future__ import annotations

@@ -105,9 +105,9 @@ SOLATTN_API int solattn_pool_qkv(const void* q, const void* k, const void* v,
  * cutoff = (sum_d qc*mean + beta * sqrt(sum_d (qc*qc)*var)) * scale, each sum over d taken
  * as eight partial sums over d = 8i + e combined in the same tree.  The cutoff is in
  * natural-log units: the attention kernel selects key block j iff dot * scale > cutoff,
- * where dot = sum_d qc[d]*kc_j[d] taken as eight partial sums p_j over d = 8i + j combined
- * as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); every operation is rounded to nearest FP32, no
- * fused multiply-add.  beta must be finite.
+ * where dot = sum_d qc[d]*kc_j[d] taken as eight partial sums p_j over d = 8i + j, each term
+ * one fused multiply-add rounded once, combined as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); every
+ * other operation is rounded to nearest FP32 without contraction.  beta must be finite.
  */
 SOLATTN_API int solattn_threshold(const void* kc, const float* qc, int64_t B, int64_t H, int64_t nqb,
                       int64_t nkb, int64_t D, float scale, float beta, float* mean, float* var,

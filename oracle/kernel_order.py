@@ -16,10 +16,11 @@ bit identity:
   mean = s1/n, var = max(s2/n - mean*mean, 0);
 * cutoff: eight partial sums over d = 8i + e (i increasing) of qc*mean and (qc*qc)*var,
   combined in the same tree; cutoff = (mu + beta*sqrt(sg)) * scale;
-* routing (fused kernel prologue): proxy = dot * scale where dot sums qc*kc as eight
-  partial sums p_j over d = 8i + j (i increasing) combined as
-  ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); exact iff proxy > cutoff (force modes and the local / sink / protected rules as in
-  ``reference.py:41-51``).
+* routing (the routing pass): proxy = dot * scale where dot sums qc*kc as eight partial sums
+  p_j over d = 8i + j (i increasing), each step one fused multiply-add
+  p_j = fma(qc[d], kc[d], p_j) rounded once (``fma32``), combined as
+  ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); exact iff proxy > cutoff (force modes and the local /
+  sink / protected rules as in ``reference.py:41-51``).
 
 Routing decisions computed here from the GPU's own pooled statistics must equal the GPU's
 bit for bit (the north-star routing criterion).
@@ -36,6 +37,30 @@ F32 = np.float32
 
 def _bf16_round(x: np.ndarray) -> np.ndarray:
     return torch.from_numpy(np.ascontiguousarray(x)).to(torch.bfloat16).float().numpy()
+
+
+def fma32(a, b, c) -> np.ndarray:
+    """IEEE fusedMultiplyAdd in float32, a*b + c rounded once to nearest (ties to even),
+    elementwise.  The product of two float32 values is exact in float64; the float64 sum s and
+    its exact error e (Knuth's TwoSum) give a*b + c = s + e exactly, and rounding s to float32
+    gives the correctly rounded result unless s lies exactly halfway between two float32
+    values while e != 0 -- then the exact value lies on e's side of that midpoint."""
+    a64 = np.asarray(a, F32).astype(np.float64)
+    b64 = np.asarray(b, F32).astype(np.float64)
+    c64 = np.asarray(c, F32).astype(np.float64)
+    p = a64 * b64
+    s = p + c64
+    bb = s - p
+    e = (p - (s - bb)) + (c64 - bb)
+    r = s.astype(F32)
+    r64 = r.astype(np.float64)
+    d = s - r64  # exact: s and r are neighbours
+    up = np.nextafter(r, F32(np.inf))
+    dn = np.nextafter(r, F32(-np.inf))
+    mid = ((d > 0) & (d == (up.astype(np.float64) - r64) / 2)) | \
+          ((d < 0) & (-d == (r64 - dn.astype(np.float64)) / 2))
+    away = mid & (e != 0) & (np.sign(e) == np.sign(d))
+    return np.where(away, np.where(d > 0, up, dn), r).astype(F32)
 
 
 def pool(x: torch.Tensor, out_bf16: bool) -> np.ndarray:
@@ -112,7 +137,7 @@ def route(qc, kc, cutoff, scale, force, local, kv_sink_blocks, q_sink_blocks, pr
         for i in range(D // 8):
             for j in range(8):
                 d = 8 * i + j
-                part[j] = part[j] + qc[:, :, :, None, d] * kc[:, :, None, :, d]
+                part[j] = fma32(qc[:, :, :, None, d], kc[:, :, None, :, d], part[j])
         dot = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]))
         sel = (dot * F32(scale)) > cutoff[..., None]
     qb = np.arange(nqb)[:, None]

@@ -160,8 +160,8 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
 }
 
 // Routing proxy dot product sum_d qbar[d] * kc[d] in a fixed order shared by every kernel and
-// by its CPU restatement: eight partial sums p_j over d = 8i + j (i increasing), each product
-// and sum rounded to nearest FP32 (no FMA contraction), then
+// by its CPU restatement: eight partial sums p_j over d = 8i + j (i increasing), each term one
+// fused multiply-add p_j = fma(qbar[d], kc[d], p_j) rounded once to nearest FP32, then
 // ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).  kcrow must be 16-byte aligned.
 __device__ __forceinline__ float routing_dot(const float* qbar, const __nv_bfloat16* kcrow, int D) {
   float p[8];
@@ -173,8 +173,8 @@ __device__ __forceinline__ float routing_dot(const float* qbar, const __nv_bfloa
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 kf = __bfloat1622float2(k2[j]);
-      p[2 * j] = __fadd_rn(p[2 * j], __fmul_rn(qbar[8 * i + 2 * j], kf.x));
-      p[2 * j + 1] = __fadd_rn(p[2 * j + 1], __fmul_rn(qbar[8 * i + 2 * j + 1], kf.y));
+      p[2 * j] = __fmaf_rn(qbar[8 * i + 2 * j], kf.x, p[2 * j]);
+      p[2 * j + 1] = __fmaf_rn(qbar[8 * i + 2 * j + 1], kf.y, p[2 * j + 1]);
     }
   }
   return __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])),
@@ -200,10 +200,10 @@ __device__ __forceinline__ void routing_dot2(const float* qa, const float* qb,
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 kf = __bfloat1622float2(k2[j]);
-      pa[2 * j] = __fadd_rn(pa[2 * j], __fmul_rn(qa[8 * i + 2 * j], kf.x));
-      pa[2 * j + 1] = __fadd_rn(pa[2 * j + 1], __fmul_rn(qa[8 * i + 2 * j + 1], kf.y));
-      pb[2 * j] = __fadd_rn(pb[2 * j], __fmul_rn(qb[8 * i + 2 * j], kf.x));
-      pb[2 * j + 1] = __fadd_rn(pb[2 * j + 1], __fmul_rn(qb[8 * i + 2 * j + 1], kf.y));
+      pa[2 * j] = __fmaf_rn(qa[8 * i + 2 * j], kf.x, pa[2 * j]);
+      pa[2 * j + 1] = __fmaf_rn(qa[8 * i + 2 * j + 1], kf.y, pa[2 * j + 1]);
+      pb[2 * j] = __fmaf_rn(qb[8 * i + 2 * j], kf.x, pb[2 * j]);
+      pb[2 * j + 1] = __fmaf_rn(qb[8 * i + 2 * j + 1], kf.y, pb[2 * j + 1]);
     }
   }
   da = __fadd_rn(__fadd_rn(__fadd_rn(pa[0], pa[1]), __fadd_rn(pa[2], pa[3])),

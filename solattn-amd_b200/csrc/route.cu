@@ -7,7 +7,7 @@
 // next 64 dims or the next 32 rows are in flight while these are used), then lane kb forms the proxies
 // of all the group's q-blocks from row kb,
 // with exactly the arithmetic of common.cuh:routing_dot (eight partial sums over d = 8i + j,
-// __fmul_rn / __fadd_rn, combined pairwise), so the decisions are bit-identical to the
+// one fused multiply-add per term, combined pairwise), so the decisions are bit-identical to the
 // per-CTA routing of the mma.sync kernel.  One ballot per q-block per 32 key blocks gives a
 // mask word: masks[((b * H + h) * nqb + qb) * nwords + kb / 32], bit kb % 32.  The word after
 // the last mask word is the fused attention kernel's work counter; the pass zeroes it.  When a
@@ -195,8 +195,9 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
   for (int w = warp_id; w < nwords; w += kRouteThreads / 32) {
     const int kb = 32 * w + lane;
     // Partial sums of dims 8i + e in pairs (e, e + 1) of packed f32x2 registers: each lane of
-    // mul.rn.f32x2 / add.rn.f32x2 rounds exactly like __fmul_rn / __fadd_rn (no contraction),
-    // so the sums are those of the scalar order with half the instructions.
+    // fma.rn.f32x2 is one fused multiply-add rounded once, exactly like fmaf, so the sums are
+    // those of the scalar order with a quarter of the instructions of separate multiplies and
+    // adds.
     uint64_t part2[kRouteQB][4];
 #pragma unroll
     for (int j = 0; j < kRouteQB; ++j)
@@ -225,10 +226,10 @@ __global__ void __launch_bounds__(kRouteThreads, 2) route_kernel(const AttnParam
           // The q-block means of dims 8i..8i+7 as four packed pairs: two 16-byte broadcast reads.
           const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(&sq[j][8 * i]);
           const ulonglong2 qb4 = *reinterpret_cast<const ulonglong2*>(&sq[j][8 * i + 4]);
-          part2[j][0] = sm100::f2_add(part2[j][0], sm100::f2_mul(qa.x, kf2[0]));
-          part2[j][1] = sm100::f2_add(part2[j][1], sm100::f2_mul(qa.y, kf2[1]));
-          part2[j][2] = sm100::f2_add(part2[j][2], sm100::f2_mul(qb4.x, kf2[2]));
-          part2[j][3] = sm100::f2_add(part2[j][3], sm100::f2_mul(qb4.y, kf2[3]));
+          part2[j][0] = sm100::f2_fma(qa.x, kf2[0], part2[j][0]);
+          part2[j][1] = sm100::f2_fma(qa.y, kf2[1], part2[j][1]);
+          part2[j][2] = sm100::f2_fma(qb4.x, kf2[2], part2[j][2]);
+          part2[j][3] = sm100::f2_fma(qb4.y, kf2[3], part2[j][3]);
         }
       }
         __syncwarp();  // every lane is done with this stage before chunk t + 2 overwrites it
