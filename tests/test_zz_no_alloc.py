@@ -125,6 +125,36 @@ def test_noalloc_status_word_is_readable():
     assert status.value == 0
 
 
+@pytest.mark.gpu
+def test_noalloc_reports_a_gather_index_outside_its_tensor():
+    """A query row index equal to the NHD tensor's row count (the Python layer rejects such
+    plans; the C entry point does not look at the indices): the kernels' own bounds checks read
+    row 0 in its place and record kStatusBadIndex (2) in the array's status word, which
+    solattn_noalloc_read_status returns as SOLATTN_ERR_DEVICE and clears."""
+    L = _lib.load()
+    N, H, D, W, n = 1024, 2, 64, 2, 256
+    gen = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn((N, H, D), generator=gen).to(torch.bfloat16).cuda() for _ in range(3))
+    rows = torch.arange(W * n, dtype=torch.int64).view(W, n)
+    rows[1, 7] = N  # outside [0, N)
+    keys = torch.arange(W * n, dtype=torch.int64).view(W, n)
+    rows, keys = rows.cuda(), keys.cuda()
+    out = torch.empty((W, n, H, D), dtype=torch.bfloat16, device="cuda")
+    counts = torch.empty((W, (n + 63) // 64, H), dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    st = (0, H * D, D)
+    rc = L.solattn_sol_forward_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), W, n, n, H, D,
+                                       *st, *st, *st, rows.data_ptr(), keys.data_ptr(), N, None,
+                                       D ** -0.5, 1.0, -1, 0, 0, out.data_ptr(),
+                                       counts.data_ptr(), stream)
+    assert rc == 0
+    status = ctypes.c_int32(0)
+    assert L.solattn_noalloc_read_status(ctypes.byref(status), stream) == -4
+    assert status.value == 2
+    assert L.solattn_noalloc_read_status(ctypes.byref(status), stream) == 0
+    assert status.value == 0
+
+
 def test_noalloc_rejects_problems_beyond_its_scratch():
     """Rejected on the host, before any GPU work: no device is needed for this check."""
     L = _lib.load()
