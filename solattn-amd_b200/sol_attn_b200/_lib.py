@@ -83,9 +83,21 @@ def check(rc: int, what: str) -> None:
         raise SolAttnError(f"{what} failed: {msg} (code {rc})")
 
 
+_LAYOUTS: dict = {}
+
+
 def workspace_layout(B, Tq, Tk, H, D):
-    """Byte offsets and total size of the scratch of one forward call."""
-    offs = [c_int64(0) for _ in range(8)]
-    total = load().solattn_workspace_layout(B, Tq, Tk, H, D, *[ctypes.byref(o) for o in offs])
-    names = ("kc", "vc", "qc", "mean", "var", "cutoff", "status", "masks")
-    return total, {n: o.value for n, o in zip(names, offs)}
+    """Byte offsets and total size of the scratch of one forward call (cached per shape and
+    library handle: the call sits on every forward's host path)."""
+    lib = load()
+    key = (id(lib), B, Tq, Tk, H, D)
+    hit = _LAYOUTS.get(key)
+    if hit is None:
+        offs = [c_int64(0) for _ in range(8)]
+        total = lib.solattn_workspace_layout(B, Tq, Tk, H, D, *[ctypes.byref(o) for o in offs])
+        names = ("kc", "vc", "qc", "mean", "var", "cutoff", "status", "masks")
+        hit = (total, {n: o.value for n, o in zip(names, offs)})
+        if len(_LAYOUTS) >= 4096:
+            _LAYOUTS.clear()
+        _LAYOUTS[key] = hit
+    return hit[0], dict(hit[1])

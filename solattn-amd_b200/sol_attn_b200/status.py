@@ -50,25 +50,28 @@ class StatusMonitor:
     def __init__(self, device_index: int):
         self.device_index = device_index
         self.host = torch.zeros(self.SLOTS, dtype=torch.int32).pin_memory()
-        self.events = [None] * self.SLOTS
+        self.words = self.host.numpy()  # the same pinned memory, read without torch indexing
+        self.host_ptr = self.host.data_ptr()
+        self.events = [None] * self.SLOTS  # created on first use, then recorded again
         self.pending = collections.deque()
         self.next = 0
         self.lock = threading.Lock()
 
     def record(self, status_ptr: int, stream: torch.cuda.Stream) -> None:
-        """Enqueue the copy of the device word at ``status_ptr`` on ``stream``."""
+        """Enqueue the copy of the device word at ``status_ptr`` on ``stream``.  A slot is
+        read only after its event completed, i.e. after the copy has overwritten it."""
         with self.lock:
             if len(self.pending) == self.SLOTS:  # every slot in flight: wait for the oldest
                 self._take(wait=True, limit=1)
             slot = self.next
             self.next = (slot + 1) % self.SLOTS
-            self.host[slot] = 0
-            rc = _lib.load().solattn_status_to_host(status_ptr, self.host.data_ptr() + 4 * slot,
+            rc = _lib.load().solattn_status_to_host(status_ptr, self.host_ptr + 4 * slot,
                                                     stream.cuda_stream)
             _lib.check(rc, "solattn_status_to_host")
-            event = torch.cuda.Event()
+            event = self.events[slot]
+            if event is None:
+                event = self.events[slot] = torch.cuda.Event()
             event.record(stream)
-            self.events[slot] = event
             self.pending.append(slot)
 
     def poll(self, wait: bool) -> None:
@@ -85,9 +88,8 @@ class StatusMonitor:
             if not wait and not event.query():
                 break
             event.synchronize()
-            value = int(self.host[slot])
+            value = int(self.words[slot])
             self.pending.popleft()
-            self.events[slot] = None
             taken += 1
             if value and not first_error:
                 first_error = value
