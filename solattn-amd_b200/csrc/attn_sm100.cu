@@ -72,6 +72,7 @@ constexpr int kKVBox = kKeys * 128;  // one 64-row x 64-column BF16 box of K or 
 constexpr int kMaxKeyBlocks = 4096;  // tile list capacity (T <= 262144 keys)
 constexpr int kClaimTiles = 8;       // late claim: the next item this many tiles before the end
 constexpr int kEarlyClaimItems = 16; // items per CTA from which the next items are claimed early
+constexpr int kOrderItemsPerCta = 2;  // items per CTA from which the routing pass sorts them
 // Tile-list entry that pads an item to an even tile count, so that every item starts at an even
 // position of the CTA's tile sequence and its tiles split between the two softmax groups by
 // their item-local parity: the result of an item then does not depend on which CTA ran it
@@ -1159,26 +1160,34 @@ cudaError_t launch_sm100(const AttnParams& p, cudaStream_t stream) {
       !make_pooled_map(&tmKC, p.kc, p.B, p.H, p.nkb, D) ||
       !make_pooled_map(&tmVC, p.vc, p.B, p.H, p.nkb, D))
     return cudaErrorInvalidValue;
-  cudaError_t err = cudaSuccess;
-  if (p.masks) {
-    err = launch_route(p, D, stream);
-    if (err != cudaSuccess) return err;
-  }
-  const size_t smem = Layout<D>::bytes(p.nkb);
   // Persistent grid: one CTA per SM, each working through items until none are left.
   const int64_t items = (int64_t)((p.nqb + 1) / 2) * p.B * p.H;
   if (items > 0x7fff0000) return cudaErrorInvalidValue;
   int dev = 0, sms = 0;
-  err = cudaGetDevice(&dev);
+  cudaError_t err = cudaGetDevice(&dev);
   if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (err != cudaSuccess) return err;
   const int64_t ctas = items < sms ? items : sms;
+  // With fewer than kOrderItemsPerCta items per CTA every CTA takes one or two items and the
+  // order cannot shorten the tail; the routing pass then skips the per-head sort (its counter,
+  // fence and the last CTA's sort are pure latency at such sizes).
+  AttnParams q = p;
+  if (items < (int64_t)kOrderItemsPerCta * ctas) {
+    q.arrive = nullptr;
+    q.stamp = nullptr;
+    q.order = nullptr;
+  }
+  if (q.masks) {
+    err = launch_route(q, D, stream);
+    if (err != cudaSuccess) return err;
+  }
+  const size_t smem = Layout<D>::bytes(q.nkb);
   // Fewer than kEarlyClaimItems items per CTA: the instantiation that claims items late.
   auto* kernel = items < (int64_t)kEarlyClaimItems * ctas ? attn_sm100_kernel<D, true>
                                                           : attn_sm100_kernel<D, false>;
   err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  kernel<<<(unsigned)ctas, kThreads, smem, stream>>>(p, tmQ, tmK, tmV, tmKC, tmVC);
+  kernel<<<(unsigned)ctas, kThreads, smem, stream>>>(q, tmQ, tmK, tmV, tmKC, tmVC);
   return cudaGetLastError();
 }
 
