@@ -76,33 +76,59 @@ def ncu_traffic(heads):
 
 
 class Clocks:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs (rank 0 only:
+    one sampler covers every GPU of the job).  The timed region of a small shard lasts a few
+    milliseconds, so the sampler runs at 50 ms and the region starts only once nvidia-smi has
+    printed its first sample; the samples from then until 120 ms after the region are kept."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, indices):
+    def __init__(self, indices, enabled=True):
         self.indices = set(indices)
+        self.enabled = enabled
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        try:  # wait (at most 5 s) for the first sample
+            import select
+            deadline = time.time() + 5.0
+            while time.time() < deadline:
+                ready, _, _ = select.select([self.proc.stdout], [], [], 0.1)
+                if ready:
+                    line = self.proc.stdout.readline()
+                    if line:
+                        self.lines.append(line)
+                    break
+                if self.proc.poll() is not None:
+                    break
+        except (OSError, ValueError):
+            pass
         return self
 
     def __exit__(self, *exc):
         self.rows = []
         if self.proc is None:
             return
-        time.sleep(0.25)
+        time.sleep(0.12)
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
-        for line in out.splitlines():
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in self.lines + (out or "").splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) == 9 and parts[0].isdigit() and int(parts[0]) in self.indices:
                 self.rows.append(parts)
@@ -285,7 +311,8 @@ def main():
           for _ in range(args.steps)]
     gpu_ids = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
     phys = gpu_ids[local_rank] if gpu_ids else local_rank
-    with Clocks([phys] if world == 1 else (gpu_ids[:world] if gpu_ids else range(world))) as clk:
+    with Clocks([phys] if world == 1 else (gpu_ids[:world] if gpu_ids else range(world)),
+                enabled=rank == 0) as clk:
         barrier()
         for s, e in ev:
             flush.zero_()  # inputs per rank can fit in L2 at N=8: flush between steps
