@@ -1,4 +1,5 @@
-// Block pooling of Q, K and V in one launch (replaces kernels.py:16-27 and 185-190).
+// Block pooling of Q, K and V in one launch (replaces kernels.py:16-27 and 185-190), and in the
+// full forward the key moments of each head (kernels.py:30-49).
 //
 // Work unit = (tensor, b, block, h).  A unit is handled by D threads laid out as 8 row
 // groups x D/8 chunk lanes; lane c of group g loads 16 bytes (8 channels) of rows
@@ -6,10 +7,15 @@
 // The 8 group partials are combined through shared memory in group order, then divided by
 // the valid row count min(64, T - 64*block) with IEEE division.  K/V means are rounded to
 // BF16 (nearest even), Q means stay FP32.  Output layout is [B, H, blocks, D].  In a ragged
-// launch batch b has its own key count (K/V blocks past it hold zeros).
+// launch batch b has its own key count (K/V blocks past it hold zeros).  A CTA pools
+// 256 / D consecutive blocks of one (b, h); grid row y is one tensor, K first.
 //
-// The pass is HBM-bound: it reads every Q/K/V element once (the 64 rows of a unit are
-// strided by sT, each row a contiguous 2*D-byte segment) and writes 1/64 of that back.
+// The pass reads every Q/K/V element once (the 64 rows of a unit are strided by sT, each row
+// a contiguous 2*D-byte segment) and writes 1/64 of that back; non-gathered rows are addressed
+// from one base pointer and a stride, so that the kernel is bound by its loads rather than by
+// instruction issue.  With fused moments (PoolParams::k_arrive) the CTA that finishes the last
+// K block of a head computes that head's mean and variance (threshold.cuh) while the Q and V
+// rows still stream.
 #include "threshold.cuh"
 
 namespace solattn {

@@ -48,6 +48,28 @@ def test_workspace_layout():
     assert total >= offs["masks"] + 24 * nqb * (nkb // 32) * 4
     assert _lib.workspace_layout(1, 100, 100, 2, 96)[0] == 0      # unsupported head dim
     assert _lib.workspace_layout(0, 100, 100, 2, 64)[0] == 0      # empty batch
+    # the status section holds the status word and two int32 [B * H] counter arrays
+    assert offs["kc"] >= 16 + 8 * 24
+    # cached per shape: the same values, and a dict the caller may change freely
+    again = _lib.workspace_layout(1, 32768, 32768, 24, 128)
+    assert again == (total, offs) and again[1] is not offs
+    offs["kc"] = -1
+    assert _lib.workspace_layout(1, 32768, 32768, 24, 128)[1]["kc"] >= 0
+
+
+@pytest.mark.parametrize("B,Tq,Tk,H", [(1, 32768, 32768, 24), (2, 8192, 5000, 8), (3, 100, 65, 5)])
+def test_mask_buffer_sections(B, Tq, Tk, H):
+    """solattn_masks_bytes = bitmask words and the work counter (padded to 16 bytes), one tile
+    list per q-block pair, then the item-order section (arrive and stamp words padded to 16
+    bytes, one order word per pair); the GPU tests read the sections with this arithmetic."""
+    nqb, nkb = -(-Tq // 64), -(-Tk // 64)
+    bh, npairs = B * H, -(-nqb // 2)
+    words = (bh * nqb * -(-nkb // 32) + 1 + 3) & ~3
+    stride = 16 + 2 * (((nkb + 63) // 64 + nkb + 1 + 7) & ~7)
+    pad = (bh + 3) & ~3
+    want = 4 * words + bh * npairs * stride + 4 * (2 * pad + bh * npairs)
+    assert _lib.load().solattn_masks_bytes(B, Tq, Tk, H) == want
+    assert stride % 16 == 0 and (4 * words) % 16 == 0  # lists and the order section 16-aligned
 
 
 def _forward(**over):
