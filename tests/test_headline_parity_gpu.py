@@ -14,7 +14,6 @@ over the 24 (the query-sink q-blocks included) and on one window of each key cou
   routing decision that differs lies within FP32 rounding of the cutoff.
 """
 
-import math
 
 import numpy as np
 import pytest

@@ -8,8 +8,6 @@ counts exactly.
 """
 
 import math
-import sys
-from pathlib import Path
 
 import numpy as np
 import pytest

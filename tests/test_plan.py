@@ -54,7 +54,6 @@ def test_indexed_rejects_invalid_controls(bad):
 
 def test_protection_matches_reference_fixture():
     ref = golden("indexed_b1")
-    from make_golden import indexed_cases  # noqa: F401  (tests/golden on sys.path via test_oracle)
     rows = torch.stack((torch.arange(231, 361), torch.arange(901, 1031)))
     keys = torch.stack((torch.cat((torch.arange(7), torch.arange(191, 703), torch.arange(1180, 1193))),
                         torch.cat((torch.arange(7), torch.arange(661, 1173), torch.arange(1180, 1193)))))
