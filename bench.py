@@ -453,7 +453,7 @@ def main():
                 "ms_per_call": e2e_ms, "h2d_bytes_per_step": h2d * world,
                 "d2h_bytes_per_step": d2h * world},
             "c5": c5,
-            "gpu_launches": st.launches() * args.steps * world,
+            "gpu_launches": st.public_launches() * args.steps * world,
             "clocks": clk.summary(),
         }
         print(json.dumps(result), flush=True)

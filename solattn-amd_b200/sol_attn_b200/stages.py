@@ -104,8 +104,14 @@ class Stages:
 
     def launches(self) -> int:
         """Kernels one run() launches: pool, threshold (threshold mode only), the routing pass
-        (tcgen05 path: BTHD inputs and at most 4096 key blocks) and the fused attention."""
-        n = 2 + (self.force == 0)
-        if not self.indexed and self.nkb <= 4096:
-            n += 1
-        return n
+        (tcgen05 path: at most 4096 key blocks) and the fused attention."""
+        return 2 + (self.force == 0) + (self.nkb <= 4096)
+
+    def public_launches(self) -> int:
+        """Kernels one public call (solattn_sol_forward) launches for this problem: pooling, the
+        routing pass and the fused attention on the tcgen05 path (the threshold is folded into
+        the first two); with more than 4096 key blocks pooling, the threshold kernel (threshold
+        mode only) and the mma.sync kernel."""
+        if self.nkb <= 4096:
+            return 3
+        return 2 + (self.force == 0)

@@ -83,3 +83,19 @@ def test_bench_receipt_rejects_bad_runs_before_touching_the_gpu(tmp_path):
     with pytest.raises(SystemExit):
         bench_receipt.main([str(out)])
     assert out.read_text() == "{}"
+
+
+def test_launch_counts_of_the_two_paths():
+    """The kernels one call launches (the bench's gpu_launches): the public call folds the
+    threshold into pooling and routing on the tcgen05 path; the stage path launches it apart;
+    beyond 4096 key blocks the mma.sync kernel routes for itself."""
+    from sol_attn_b200.stages import Stages
+    q, k, v = (torch.zeros((1, 4096, 2, 64), dtype=torch.bfloat16) for _ in range(3))
+    st = Stages(q, k, v, beta=1.0)
+    assert (st.launches(), st.public_launches()) == (4, 3)
+    st = Stages(q, k, v, beta=math.inf)
+    assert (st.launches(), st.public_launches()) == (3, 3)
+    t = 64 * 4097
+    q, k, v = (torch.zeros((1, t, 1, 64), dtype=torch.bfloat16) for _ in range(3))
+    st = Stages(q, k, v, beta=1.0)
+    assert (st.launches(), st.public_launches()) == (3, 3)
