@@ -13,9 +13,10 @@
 // the last mask word is the fused attention kernel's work counter; the pass zeroes it.  When a
 // list buffer is given the pass also builds every q-block pair's tile list for the fused kernel
 // (common.cuh: build_item_list) and writes the exact-block counts, so that no attention CTA
-// spends time on either between two items.  The last CTA of a head to finish its lists then
-// sorts the head's q-block pairs (after the sink pairs) by tile count, longest first, for the
-// fused kernel's work claims (AttnParams::order): handed out longest first within each head,
+// spends time on either between two items.  With at least two items per attention CTA (the
+// launcher leaves AttnParams::arrive null otherwise) the last CTA of a head to finish its lists
+// then sorts the head's q-block pairs (after the sink pairs) by tile count, longest first, for
+// the fused kernel's work claims (AttnParams::order): handed out longest first within each head,
 // the last items of a launch are its shortest, which shortens the tail in which some CTAs
 // still run their last item while the others have none left.  Ties keep no fixed order; the
 // results do not depend on the order in which items run.
